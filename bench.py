@@ -1,0 +1,449 @@
+#!/usr/bin/env python
+"""Benchmark: one differentiable-voxelization training step.
+
+A step = projection (optim_to_render) -> binning -> voxelize forward ->
+L1 loss against a phantom -> backward (voxelize backward, projection
+backward), the path of the reference's own speed benchmark. Workload at
+N = 1 is BASELINE configuration 2: 256^3 volume, 100k Gaussians,
+64-ellipsoid phantom (synthetic, seeded). At N > 1 the volume is z-slab
+sharded with per-GPU work fixed (weak scaling): a (256N, 256, 256) volume
+with N x 100k Gaussians, one 256^3 slab per rank, one NCCL all-reduce of the
+per-Gaussian gradients per step.
+
+Metric: Gaussian-voxel evaluations per second over the whole step, counting
+each (Gaussian, voxel) pair once in the forward and once in the backward
+pass (E from the binning: sum over tiles of Gaussians x voxels).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "Gaussian-voxel evals/s, fwd+bwd step, 256^3 vol / 100k Gaussians per GPU"
+UNIT = "evals/s"
+SMS = 148
+MUFU_PER_CLK = 16          # MUFU.EX2 throughput per SM per clock
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+# ----------------------------------------------------------------- helpers
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.seek(0)
+        rows = [r.split(", ") for r in self.file.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for name, flag in zip(names, r[5:9]):
+                    if flag.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    if world != gpus:
+        log(f"note: --gpus {gpus} but WORLD_SIZE {world}; using {world}")
+    return world, rank, local
+
+
+def workload(world: int):
+    from gs_voxelizer_b200.workloads import CONFIGS, Config
+    base = CONFIGS["step256"]
+    if world == 1:
+        return base
+    Z, Y, X = base.vol
+    return Config(f"step256-weak{world}", (Z * world, Y, X), base.n * world,
+                  pos=base.pos, scale=base.scale, intensity=base.intensity,
+                  ellipsoids=base.ellipsoids * world,
+                  world=(float(world), 1.0, 1.0),
+                  center=(world / 2.0, 0.5, 0.5), seed=base.seed)
+
+
+def make_inputs(cfg, world):
+    from gs_voxelizer_b200.workloads import gaussians
+    pos, scale, quat, inten = gaussians(cfg)
+    if world > 1:  # z spans the stacked volume
+        lo, hi = cfg.pos
+        rng = np.random.default_rng(cfg.seed + 1)
+        pos[:, 2] = rng.uniform(lo, world - (1.0 - hi), size=cfg.n).astype(np.float32)
+    return pos, scale, quat, inten
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------- step builders
+
+class Step:
+    """Holds device-resident leaves, target and the API used per step."""
+
+    def __init__(self, impl, cfg, world, rank, inputs):
+        self.impl, self.cfg, self.world, self.rank = impl, cfg, world, rank
+        dev = torch.device("cuda")
+        self.host = [torch.from_numpy(a).pin_memory() for a in inputs]
+        self.leaves = [h.to(dev).requires_grad_(True) for h in self.host]
+        from gs_voxelizer_b200.workloads import phantom
+        from gs_voxelizer_b200.slab import SlabPlan, slab_bounds
+        tz0, tz1 = slab_bounds(cfg.vol, world, rank)
+        self.plan = SlabPlan(cfg.vol, tz0, tz1)
+        self.target = phantom(cfg, device=dev, z_range=(self.plan.z_begin, self.plan.z_end))
+        self.nvox_global = cfg.vol[0] * cfg.vol[1] * cfg.vol[2] * cfg.channels
+        self.in_bytes = sum(h.numel() * h.element_size() for h in self.host)
+        if impl == "reference":
+            from oracle import ref_api
+            self.api = ref_api
+        else:
+            from gs_voxelizer_b200 import optim_to_render, slab, voxelize
+            self.o2r = optim_to_render.optim_to_render
+            self.vox = voxelize.voxelize_gaussians
+            self.vox_slab = slab.voxelize_gaussians_slab
+
+    def forward(self):
+        cfg = self.cfg
+        pos, scale, quat, inten = self.leaves
+        if self.impl == "reference":
+            pr, cq, tmin, tmax, nt = self.api.optim_to_render(
+                pos, scale, quat, inten, cfg.vol, cfg.world, cfg.center)
+            vol = self.api.voxelize_gaussians(pr, cq, inten, cfg.vol, tmin,
+                                              tmax, nt, True)
+        else:
+            pr, cq, tmin, tmax, nt = self.o2r(pos, scale, quat, inten, cfg.vol,
+                                              cfg.world, cfg.center)
+            if self.world == 1:
+                vol = self.vox(pr, cq, inten, cfg.vol, tmin, tmax, nt, True)
+            else:
+                vol = self.vox_slab(pr, cq, inten, self.plan, tmin, tmax)
+        # slab L1 loss normalised by the global voxel count (sums to the
+        # full-volume torch.nn.functional.l1_loss)
+        loss = torch.nn.functional.l1_loss(vol, self.target, reduction="sum") / self.nvox_global
+        return loss
+
+    def zero_grad(self):
+        for t in self.leaves:
+            t.grad = None
+
+    def step(self):
+        self.zero_grad()
+        loss = self.forward()
+        loss.backward()
+        return loss
+
+    def step_e2e(self):
+        """Public-API step with the inputs copied from pinned host memory and
+        the loss read back to the host."""
+        with torch.no_grad():
+            for d, h in zip(self.leaves, self.host):
+                d.copy_(h, non_blocking=True)
+        loss = self.step()
+        return float(loss.detach().item())
+
+    def evaluations(self):
+        """E for this rank's slab (forward pass), from a fresh binning."""
+        from gs_voxelizer_b200.workloads import evaluations
+        from gs_voxelizer_b200 import cuda as C
+        cfg = self.cfg
+        with torch.no_grad():
+            pos, scale, quat, inten = self.leaves
+            pr, cq, tmin, tmax, nt = C.optim_to_render_forward(
+                cfg.n, pos, scale, quat, inten, cfg.vol, cfg.world, cfg.center)
+            ids, bins = self.plan.bin(tmin, tmax)
+            return evaluations(bins, cfg.vol, (self.plan.tz0, self.plan.tz1)), ids.numel()
+
+
+# ------------------------------------------------------------------ timing
+
+def time_steps(fn, steps, flush):
+    """Per-step CUDA-event timing with an L2 flush between steps (untimed)."""
+    total = 0.0
+    per = []
+    for _ in range(steps):
+        flush.fill_(1.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e)
+        per.append(ms)
+        total += ms
+    return total, per
+
+
+def time_fwd_bwd(step_obj, steps, flush):
+    fwd, bwd = [], []
+    for _ in range(steps):
+        flush.fill_(1.0)
+        step_obj.zero_grad()
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        loss = step_obj.forward()
+        b.record()
+        loss.backward()
+        c.record()
+        c.synchronize()
+        fwd.append(a.elapsed_time(b))
+        bwd.append(b.elapsed_time(c))
+    return statistics.median(fwd), statistics.median(bwd)
+
+
+def time_main_kernels(step_obj, steps, flush):
+    """Average duration of the main forward / per-Gaussian backward kernels,
+    from CUDA events the library records around them on their stream."""
+    from gs_voxelizer_b200._lib import lib
+    res = {}
+    for which, name in ((0, "forward"), (1, "backward")):
+        ts = []
+        for _ in range(steps):
+            flush.fill_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            lib.gsv_profile_kernel(which, s.cuda_event, e.cuda_event)
+            step_obj.step()
+            lib.gsv_profile_kernel(which, None, None)
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        res[name] = statistics.mean(ts)
+    return res
+
+
+def cpu_baseline(cfg, inputs, budget_s=12.0):
+    """The C oracle (oracle/gsv_oracle.c, OpenMP) on a bounded sample of the
+    same workload: consecutive 2-tile-layer z-slabs of the volume, fwd + L1 +
+    bwd, until the time budget is used or the whole volume is done."""
+    from oracle import oracle as O
+    from gs_voxelizer_b200.workloads import evaluations, phantom
+    pos, scale, quat, inten = inputs
+    t0 = time.perf_counter()
+    pr, cq, tmin, tmax, nt = O.optim_to_render_forward(
+        pos, scale, quat, inten, cfg.vol, cfg.world, cfg.center)
+    t_proj = time.perf_counter() - t0
+    Tz = (cfg.vol[0] + 7) // 8
+    evals, secs, layers = 0, t_proj, 0
+    tz0 = 0
+    while secs < budget_s and tz0 < Tz:
+        tz1 = min(Tz, tz0 + 2)
+        target = phantom(cfg, device="cpu", z_range=(8 * tz0, min(cfg.vol[0], 8 * tz1))).numpy()
+        t0 = time.perf_counter()
+        ids, bins = O.bin_and_sort_gaussians(tmin, tmax, cfg.vol, tile_z=(tz0, tz1))
+        vol = O.voxelize_forward(cfg.vol, ids, bins, pr, cq, inten, tile_z=(tz0, tz1))
+        _, g = O.l1_loss_and_grad(vol, target)
+        gp, gc, gi = O.voxelize_backward(cfg.vol, tmin, tmax, pr, cq, inten, g,
+                                         tile_z=(tz0, tz1))
+        secs += time.perf_counter() - t0
+        evals += 2 * evaluations(torch.from_numpy(bins), cfg.vol, (tz0, tz1))
+        layers += tz1 - tz0
+        tz0 = tz1
+    return {"value": evals / secs, "unit": UNIT, "cores": O.num_threads(),
+            "kind": "port",
+            "sample": f"C oracle (OpenMP), {layers} of {Tz} tile layers of the "
+                      f"same workload (projection of all {cfg.n} Gaussians + "
+                      f"slab binning, fwd, L1, bwd), {secs:.1f} s"}
+
+
+# -------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: 128^3, 25k Gaussians, 3 steps")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world, rank, local = setup_dist(args.gpus)
+    impl = args.impl
+    if impl == "reference" and rank != 0:
+        return  # the reference is single-GPU: rank 0 alone runs it
+    if impl == "reference":
+        world = 1
+        from oracle import ref_api
+        if not ref_api.available():
+            print(json.dumps({"impl": "reference",
+                              "unavailable": "reference extension not built (oracle/_ref)"}))
+            return
+
+    cfg = workload(world)
+    if args.small:
+        from gs_voxelizer_b200.workloads import Config
+        cfg = Config("small128", (128, 128, 128), 25_000, pos=cfg.pos,
+                     scale=(0.004, 0.04), intensity=cfg.intensity, ellipsoids=16)
+    inputs = make_inputs(cfg, world)
+    st = Step(impl, cfg, world, rank, inputs)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    E, n_isect = st.evaluations()
+    E_total = int(sum_over_ranks(float(E), world))
+    evals_per_step = 2 * E_total
+
+    for _ in range(args.warmup):
+        st.step()
+    barrier(world)
+
+    from gs_voxelizer_b200._lib import lib
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = lib.gsv_launch_count()
+    barrier(world)
+    total_ms, per = time_steps(st.step, args.steps, flush)
+    barrier(world)
+    launches = lib.gsv_launch_count() - launches0
+    clocks = sampler.stop()
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    value = evals_per_step / (ms_per_step / 1e3)
+
+    # end to end through the public API with host buffers
+    for _ in range(2):
+        st.step_e2e()
+    barrier(world)
+    e2e_ms, _ = time_steps(st.step_e2e, args.steps, flush)
+    e2e_ms = max_over_ranks(e2e_ms, world) / args.steps
+
+    fwd_ms, bwd_ms = time_fwd_bwd(st, max(3, args.steps // 2), flush)
+    fwd_ms, bwd_ms = max_over_ranks(fwd_ms, world), max_over_ranks(bwd_ms, world)
+
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded Gaussians + ellipsoid phantom)",
+        "config": {"workload": cfg.name, "vol_zyx": list(cfg.vol),
+                   "gaussians": cfg.n, "channels": cfg.channels,
+                   "intersections_per_gpu": n_isect,
+                   "evals_per_step": evals_per_step,
+                   "parallelism": f"z-slab x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed between timed steps (256 MB write)",
+                   "loss": "L1 vs phantom"},
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "e2e": {"value": evals_per_step / (e2e_ms / 1e3), "unit": UNIT,
+                "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": st.in_bytes, "d2h_bytes_per_step": 4},
+        "clocks": clocks,
+    }
+    if impl == "reference":
+        out["impl"] = "reference"
+        out["reference_build"] = ("reference CUDA sources compiled for sm_100a "
+                                  "(oracle/build_ref.py), run on the same GPU")
+        out["gpu_launches"] = None
+    else:
+        out["impl"] = "ours"
+        out["gpu_launches"] = int(launches)
+        kt = time_main_kernels(st, max(3, args.steps // 2), flush)
+        kt = {k: max_over_ranks(v, world) for k, v in kt.items()}
+        clk = (clocks or {}).get("sm_max_mhz") or 1965.0
+        peak = SMS * MUFU_PER_CLK * clk * 1e6 / 1e9  # Geval/s
+        dom = max(kt, key=kt.get)
+        achieved = E / (kt[dom] / 1e3) / 1e9
+        out["kernel_ms"] = kt
+        out["roofline"] = {
+            "bound": "mufu", "kernel": f"voxelize {dom}",
+            "achieved": achieved, "peak": peak, "unit": "Geval/s",
+            "frac": achieved / peak, "traffic": None,
+            "note": ("one MUFU.EX2 per Gaussian-voxel evaluation at 16/clk/SM "
+                     "x 148 SMs x max SM clock; E per launch = this rank's "
+                     "forward evaluations")}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small:
+        try:
+            out["cpu_baseline"] = cpu_baseline(cfg, inputs)
+        except Exception as exc:  # reported, not fatal
+            out["cpu_baseline"] = {"error": str(exc)}
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,446 @@
+// extern "C" entry points declared in include/gsvox.h: argument checks,
+// workspace layout and dispatch to the kernels. No device allocation happens
+// here; errors are returned as status codes with a per-thread message.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/gsvox.h"
+#include "common.cuh"
+
+namespace gsv {
+cudaError_t launch_project_fwd(int n, int channels, const float *pos3d,
+                               const float *scale3d, const float *quat,
+                               const float *intensities, const int vol[3],
+                               const float world[3], const float center[3],
+                               float *pos_radii, float *conics, int *tile_min,
+                               int *tile_max, int *num_tiles,
+                               cudaStream_t stream);
+cudaError_t launch_project_bwd(int n, const float *pos3d, const float *scale3d,
+                               const float *quat, const int vol[3],
+                               const float world[3], const float *pos_radii_grad,
+                               const float *conics_grad, const float *pos_radii,
+                               float *pos_grad, float *scale_grad,
+                               float *quat_grad, cudaStream_t stream);
+size_t bin_workspace_bytes(long long ntiles, long long nisect);
+cudaError_t launch_binning(int n, long long nisect, const int *tmin,
+                           const int *tmax, int Tx, int Ty, int tz0, int tz1,
+                           int *ids_out, int *tile_bins, void *ws,
+                           cudaStream_t stream);
+cudaError_t launch_count_slab_pairs(int n, const int *tmin, const int *tmax,
+                                    int tz0, int tz1, long long *out,
+                                    cudaStream_t stream);
+size_t vox_workspace_bytes(long long n, int channels, long long ntiles,
+                           long long nisect);
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
+                               const int *tile_bins, const float *pos_radii,
+                               const float *conics, const float *intens,
+                               float *out, void *ws, cudaStream_t stream);
+cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
+                                      long long nisect, const int *ids,
+                                      const int *tile_bins,
+                                      const float *pos_radii,
+                                      const float *conics,
+                                      const float *intens, const float *grad,
+                                      float *pos_grad, float *conic_grad,
+                                      float *int_grad, void *ws,
+                                      cudaStream_t stream);
+cudaError_t launch_vox_backward_voxel(const Geom &g, int C, int n,
+                                      long long nisect, const int *ids,
+                                      const int *tile_bins,
+                                      const float *pos_radii,
+                                      const float *conics,
+                                      const float *intens, const float *grad,
+                                      float *pos_grad, float *conic_grad,
+                                      float *int_grad, void *ws,
+                                      cudaStream_t stream);
+void enable_large_smem();
+}  // namespace gsv
+
+namespace gsv {
+static std::atomic<unsigned long long> g_launches{0};
+void count_launches(int k) { g_launches.fetch_add((unsigned long long)k); }
+
+static thread_local cudaEvent_t g_prof[3][2] = {};
+void profile_mark(int kind, bool stop, cudaStream_t stream) {
+    cudaEvent_t e = g_prof[kind][stop ? 1 : 0];
+    if (e) cudaEventRecord(e, stream);
+}
+}  // namespace gsv
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_status(cudaError_t err, const char *where) {
+    if (err == cudaSuccess) return GSV_OK;
+    return fail(GSV_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)err,
+                cudaGetErrorString(err));
+}
+
+bool check_vol(const int32_t v[3], const char *fn) {
+    if (!v) {
+        fail(GSV_ERR_INVALID_ARGUMENT, "%s: vol_size_voxel is null", fn);
+        return false;
+    }
+    for (int i = 0; i < 3; ++i) {
+        if (v[i] <= 0) {
+            fail(GSV_ERR_INVALID_ARGUMENT,
+                 "%s: vol_size_voxel must be positive, got (%d, %d, %d)", fn,
+                 v[0], v[1], v[2]);
+            return false;
+        }
+    }
+    return true;
+}
+
+bool check_slab(const gsv::Geom &g, const char *fn) {
+    if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) {
+        fail(GSV_ERR_INVALID_ARGUMENT,
+             "%s: tile z range [%d, %d) is outside [0, %d)", fn, g.tz0, g.tz1,
+             g.Tz);
+        return false;
+    }
+    return true;
+}
+
+#define GSV_REQUIRE(cond, code, ...)            \
+    do {                                        \
+        if (!(cond)) return fail(code, __VA_ARGS__); \
+    } while (0)
+
+cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+int binning_impl(const char *fn, int32_t n, int64_t nisect,
+                 const int32_t *tile_min, const int32_t *tile_max,
+                 const gsv::Geom &g, int32_t *ids_out, int32_t *bins_out,
+                 void *ws, size_t ws_bytes, void *stream) {
+    GSV_REQUIRE(n >= 0 && nisect >= 0, GSV_ERR_INVALID_ARGUMENT,
+                "%s: negative size (num_gaussians=%d, num_intersects=%lld)",
+                fn, n, (long long)nisect);
+    GSV_REQUIRE(nisect <= INT32_MAX, GSV_ERR_SIZE_OVERFLOW,
+                "%s: num_intersects=%lld exceeds the int32 tile_bins format",
+                fn, (long long)nisect);
+    const long long ntiles = g.slab_tiles();
+    GSV_REQUIRE(ntiles <= INT32_MAX, GSV_ERR_SIZE_OVERFLOW,
+                "%s: %lld tiles exceed the int32 tile id format", fn, ntiles);
+    GSV_REQUIRE(ntiles == 0 || bins_out, GSV_ERR_INVALID_ARGUMENT,
+                "%s: tile_bins is null", fn);
+    GSV_REQUIRE(nisect == 0 || (ids_out && tile_min && tile_max),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null input/output pointer", fn);
+    const size_t need = gsv::bin_workspace_bytes(ntiles, nisect);
+    GSV_REQUIRE(ws_bytes >= need && (need == 0 || ws),
+                GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
+                need);
+    gsv::enable_large_smem();
+    return cuda_status(gsv::launch_binning(n, nisect, tile_min, tile_max,
+                                           g.Tx, g.Ty, g.tz0, g.tz1, ids_out,
+                                           bins_out, ws, as_stream(stream)),
+                       fn);
+}
+
+int vox_common_checks(const char *fn, const gsv::Geom &g, int32_t C,
+                      int32_t n, int64_t nisect, const int32_t *ids,
+                      const int32_t *bins, const float *pos, const float *con,
+                      const float *inten, size_t ws_bytes, void *ws) {
+    GSV_REQUIRE(C >= 1 && C <= 4, GSV_ERR_UNSUPPORTED_CHANNELS,
+                "%s: %d channels requested, 1..4 supported", fn, C);
+    GSV_REQUIRE(n >= 0 && nisect >= 0, GSV_ERR_INVALID_ARGUMENT,
+                "%s: negative size", fn);
+    GSV_REQUIRE(nisect <= INT32_MAX, GSV_ERR_SIZE_OVERFLOW,
+                "%s: num_intersects exceeds int32", fn);
+    GSV_REQUIRE(g.slab_tiles() <= INT32_MAX, GSV_ERR_SIZE_OVERFLOW,
+                "%s: tile count exceeds int32", fn);
+    if (nisect > 0) {
+        GSV_REQUIRE(ids && bins && pos && con && inten,
+                    GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
+    }
+    const size_t need =
+        gsv::vox_workspace_bytes(n, C, g.slab_tiles(), nisect);
+    GSV_REQUIRE(ws_bytes >= need && ws, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
+                need);
+    return GSV_OK;
+}
+
+int forward_impl(const char *fn, const gsv::Geom &g, int32_t C, int32_t n,
+                 int64_t nisect, const int32_t *ids, const int32_t *bins,
+                 const float *pos, const float *con, const float *inten,
+                 float *out, void *ws, size_t ws_bytes, void *stream) {
+    if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
+                               ws_bytes, ws);
+    if (st) return st;
+    const long long nvox =
+        (long long)(g.z_end() - g.z_begin()) * g.Y * g.X * C;
+    GSV_REQUIRE(out || nvox == 0, GSV_ERR_INVALID_ARGUMENT, "%s: out_vol is null",
+                fn);
+    if (nisect == 0) {
+        return cuda_status(cudaMemsetAsync(out, 0, sizeof(float) * nvox,
+                                           as_stream(stream)),
+                           fn);
+    }
+    return cuda_status(gsv::launch_vox_forward(g, C, n, ids, bins, pos, con,
+                                               inten, out, ws,
+                                               as_stream(stream)),
+                       fn);
+}
+
+int backward_impl(const char *fn, bool per_gaussian, const gsv::Geom &g,
+                  int32_t C, int32_t n, int64_t nisect, const int32_t *ids,
+                  const int32_t *bins, const float *pos, const float *con,
+                  const float *inten, const float *grad, float *pos_grad,
+                  float *con_grad, float *int_grad, void *ws, size_t ws_bytes,
+                  void *stream) {
+    if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
+                               ws_bytes, ws);
+    if (st) return st;
+    GSV_REQUIRE(n == 0 || (pos_grad && con_grad && int_grad),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null gradient output", fn);
+    GSV_REQUIRE(nisect == 0 || grad, GSV_ERR_INVALID_ARGUMENT,
+                "%s: vol_grad_in is null", fn);
+    cudaError_t err =
+        per_gaussian
+            ? gsv::launch_vox_backward_gauss(g, C, n, nisect, ids, bins, pos,
+                                             con, inten, grad, pos_grad,
+                                             con_grad, int_grad, ws,
+                                             as_stream(stream))
+            : gsv::launch_vox_backward_voxel(g, C, n, nisect, ids, bins, pos,
+                                             con, inten, grad, pos_grad,
+                                             con_grad, int_grad, ws,
+                                             as_stream(stream));
+    return cuda_status(err, fn);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *gsv_last_error(void) { return g_last_error.c_str(); }
+
+const char *gsv_version(void) { return "0.1.0"; }
+
+uint64_t gsv_launch_count(void) { return gsv::g_launches.load(); }
+
+int gsv_profile_kernel(int32_t which, void *start_event, void *stop_event) {
+    GSV_REQUIRE(which >= 0 && which < 3, GSV_ERR_INVALID_ARGUMENT,
+                "gsv_profile_kernel: which=%d not in 0..2", which);
+    gsv::g_prof[which][0] = static_cast<cudaEvent_t>(start_event);
+    gsv::g_prof[which][1] = static_cast<cudaEvent_t>(stop_event);
+    return GSV_OK;
+}
+
+int gsv_optim_to_render_forward(int32_t n, int32_t C, const float *pos3d,
+                                const float *scale3d, const float *quat,
+                                const float *intensities,
+                                const int32_t vol[3], const float world[3],
+                                const float center[3], float *pos_radii,
+                                float *conics, int32_t *tile_min,
+                                int32_t *tile_max, int32_t *num_tiles,
+                                void *stream) {
+    const char *fn = "gsv_optim_to_render_forward";
+    GSV_REQUIRE(C >= 1 && C <= 4, GSV_ERR_UNSUPPORTED_CHANNELS,
+                "%s: %d channels requested, 1..4 supported", fn, C);
+    GSV_REQUIRE(n >= 0, GSV_ERR_INVALID_ARGUMENT, "%s: negative size", fn);
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    GSV_REQUIRE(world && center, GSV_ERR_INVALID_ARGUMENT,
+                "%s: null volume description", fn);
+    if (n == 0) return GSV_OK;
+    GSV_REQUIRE(pos3d && scale3d && quat && intensities && pos_radii &&
+                    conics && tile_min && tile_max && num_tiles,
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(
+        gsv::launch_project_fwd(n, C, pos3d, scale3d, quat, intensities, vol,
+                                world, center, pos_radii, conics, tile_min,
+                                tile_max, num_tiles, as_stream(stream)),
+        fn);
+}
+
+int gsv_optim_to_render_backward(int32_t n, const float *pos3d,
+                                 const float *scale3d, const float *quat,
+                                 const int32_t vol[3], const float world[3],
+                                 const float center[3],
+                                 const float *pos_radii_grad,
+                                 const float *conics_grad,
+                                 const float *pos_radii, float *pos_grad,
+                                 float *scale_grad, float *quat_grad,
+                                 void *stream) {
+    const char *fn = "gsv_optim_to_render_backward";
+    GSV_REQUIRE(n >= 0, GSV_ERR_INVALID_ARGUMENT, "%s: negative size", fn);
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    GSV_REQUIRE(world && center, GSV_ERR_INVALID_ARGUMENT,
+                "%s: null volume description", fn);
+    if (n == 0) return GSV_OK;
+    GSV_REQUIRE(pos3d && scale3d && quat && pos_radii_grad && conics_grad &&
+                    pos_radii && pos_grad && scale_grad && quat_grad,
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(
+        gsv::launch_project_bwd(n, pos3d, scale3d, quat, vol, world,
+                                pos_radii_grad, conics_grad, pos_radii,
+                                pos_grad, scale_grad, quat_grad,
+                                as_stream(stream)),
+        fn);
+}
+
+size_t gsv_bin_and_sort_workspace_bytes(int32_t n, int64_t nisect,
+                                        const int32_t vol[3]) {
+    (void)n;
+    if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
+    const gsv::Geom g = gsv::make_geom(vol);
+    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect);
+}
+
+int gsv_bin_and_sort_gaussians(int32_t n, int64_t nisect,
+                               const int32_t *tile_min,
+                               const int32_t *tile_max,
+                               const int32_t *cum_tiles_hit,
+                               const int32_t vol[3], int32_t *ids_out,
+                               int32_t *bins_out, void *ws, size_t ws_bytes,
+                               void *stream) {
+    const char *fn = "gsv_bin_and_sort_gaussians";
+    (void)cum_tiles_hit;
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    const gsv::Geom g = gsv::make_geom(vol);
+    return binning_impl(fn, n, nisect, tile_min, tile_max, g, ids_out,
+                        bins_out, ws, ws_bytes, stream);
+}
+
+size_t gsv_bin_and_sort_slab_workspace_bytes(int32_t n, int64_t nisect,
+                                             const int32_t vol[3],
+                                             int32_t tz0, int32_t tz1) {
+    (void)n;
+    if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
+    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect);
+}
+
+int gsv_bin_and_sort_gaussians_slab(int32_t n, int64_t nisect,
+                                    const int32_t *tile_min,
+                                    const int32_t *tile_max,
+                                    const int32_t vol[3], int32_t tz0,
+                                    int32_t tz1, int32_t *ids_out,
+                                    int32_t *bins_out, void *ws,
+                                    size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_bin_and_sort_gaussians_slab";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return binning_impl(fn, n, nisect, tile_min, tile_max, g, ids_out,
+                        bins_out, ws, ws_bytes, stream);
+}
+
+int gsv_count_slab_intersects(int32_t n, const int32_t *tile_min,
+                              const int32_t *tile_max, int32_t tz0,
+                              int32_t tz1, int64_t *count_out, void *stream) {
+    const char *fn = "gsv_count_slab_intersects";
+    GSV_REQUIRE(n >= 0 && tz0 >= 0 && tz1 >= tz0, GSV_ERR_INVALID_ARGUMENT,
+                "%s: bad arguments", fn);
+    GSV_REQUIRE(count_out && (n == 0 || (tile_min && tile_max)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(
+        gsv::launch_count_slab_pairs(n, tile_min, tile_max, tz0, tz1,
+                                     reinterpret_cast<long long *>(count_out),
+                                     as_stream(stream)),
+        fn);
+}
+
+size_t gsv_voxelize_workspace_bytes(int32_t n, int32_t C, int64_t nisect,
+                                    const int32_t vol[3]) {
+    if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
+    if (C < 1 || C > 4) return 0;
+    const gsv::Geom g = gsv::make_geom(vol);
+    return gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(),
+                                    nisect < 0 ? 0 : nisect);
+}
+
+size_t gsv_voxelize_slab_workspace_bytes(int32_t n, int32_t C, int64_t nisect,
+                                         const int32_t vol[3], int32_t tz0,
+                                         int32_t tz1) {
+    if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
+    if (C < 1 || C > 4) return 0;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
+    return gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(),
+                                    nisect < 0 ? 0 : nisect);
+}
+
+int gsv_voxelize_forward(const int32_t vol[3], int32_t C, int32_t n,
+                         int64_t nisect, const int32_t *ids,
+                         const int32_t *bins, const float *pos,
+                         const float *con, const float *inten, float *out,
+                         void *ws, size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_voxelize_forward";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return forward_impl(fn, gsv::make_geom(vol), C, n, nisect, ids, bins, pos,
+                        con, inten, out, ws, ws_bytes, stream);
+}
+
+int gsv_voxelize_forward_slab(const int32_t vol[3], int32_t tz0, int32_t tz1,
+                              int32_t C, int32_t n, int64_t nisect,
+                              const int32_t *ids, const int32_t *bins,
+                              const float *pos, const float *con,
+                              const float *inten, float *out, void *ws,
+                              size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_voxelize_forward_slab";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return forward_impl(fn, gsv::make_geom(vol, tz0, tz1), C, n, nisect, ids,
+                        bins, pos, con, inten, out, ws, ws_bytes, stream);
+}
+
+int gsv_voxelize_backward_per_gaussian(
+    const int32_t vol[3], int32_t C, int32_t n, int64_t nisect,
+    const int32_t *ids, const int32_t *bins, const float *pos,
+    const float *con, const float *inten, const float *grad, float *pos_grad,
+    float *con_grad, float *int_grad, void *ws, size_t ws_bytes,
+    void *stream) {
+    const char *fn = "gsv_voxelize_backward_per_gaussian";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return backward_impl(fn, true, gsv::make_geom(vol), C, n, nisect, ids,
+                         bins, pos, con, inten, grad, pos_grad, con_grad,
+                         int_grad, ws, ws_bytes, stream);
+}
+
+int gsv_voxelize_backward_per_gaussian_slab(
+    const int32_t vol[3], int32_t tz0, int32_t tz1, int32_t C, int32_t n,
+    int64_t nisect, const int32_t *ids, const int32_t *bins, const float *pos,
+    const float *con, const float *inten, const float *grad, float *pos_grad,
+    float *con_grad, float *int_grad, void *ws, size_t ws_bytes,
+    void *stream) {
+    const char *fn = "gsv_voxelize_backward_per_gaussian_slab";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return backward_impl(fn, true, gsv::make_geom(vol, tz0, tz1), C, n, nisect,
+                         ids, bins, pos, con, inten, grad, pos_grad, con_grad,
+                         int_grad, ws, ws_bytes, stream);
+}
+
+int gsv_voxelize_backward(const int32_t vol[3], int32_t C, int32_t n,
+                          int64_t nisect, const int32_t *ids,
+                          const int32_t *bins, const float *pos,
+                          const float *con, const float *inten,
+                          const float *grad, float *pos_grad, float *con_grad,
+                          float *int_grad, void *ws, size_t ws_bytes,
+                          void *stream) {
+    const char *fn = "gsv_voxelize_backward";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    return backward_impl(fn, false, gsv::make_geom(vol), C, n, nisect, ids,
+                         bins, pos, con, inten, grad, pos_grad, con_grad,
+                         int_grad, ws, ws_bytes, stream);
+}
+
+}  // extern "C"

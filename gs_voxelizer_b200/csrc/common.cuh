@@ -1,0 +1,96 @@
+// Shared definitions of the sm_100a voxelization kernels.
+#pragma once
+
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace gsv {
+
+// Tile edge in voxels, fixed by the reference's binning format
+// (gs_voxelizer/cuda/config.h:1-4): tile ids and tile_bins depend on it.
+constexpr int kTile = 8;
+constexpr int kTileVoxels = kTile * kTile * kTile;
+constexpr int kMaxChannels = 4;
+constexpr int kSMs = 148;
+
+// Geometry of the volume, or of a z-slab of it, as the kernels see it.
+// The full volume is the slab [0, Tz).
+struct Geom {
+    int X, Y, Z;        // full-volume voxel extents
+    int Tx, Ty, Tz;     // full-volume tile extents
+    int tz0, tz1;       // tile-z range of the slab
+    __host__ __device__ int slab_tiles_z() const { return tz1 - tz0; }
+    __host__ __device__ int64_t slab_tiles() const {
+        return (int64_t)(tz1 - tz0) * Ty * Tx;
+    }
+    // voxel z range of the slab's output buffer
+    __host__ __device__ int z_begin() const { return tz0 * kTile; }
+    __host__ __device__ int z_end() const { return min(Z, tz1 * kTile); }
+};
+
+inline Geom make_geom(const int32_t vol_zyx[3], int tz0 = 0, int tz1 = -1) {
+    Geom g;
+    g.Z = vol_zyx[0];
+    g.Y = vol_zyx[1];
+    g.X = vol_zyx[2];
+    g.Tx = (g.X + kTile - 1) / kTile;
+    g.Ty = (g.Y + kTile - 1) / kTile;
+    g.Tz = (g.Z + kTile - 1) / kTile;
+    g.tz0 = tz0;
+    g.tz1 = tz1 < 0 ? g.Tz : tz1;
+    return g;
+}
+
+// Running count of kernels this library has launched (gsv_launch_count()).
+void count_launches(int k);
+
+// Optional CUDA events recorded right before / after the main voxelization
+// kernels (gsv_profile_kernel()); no-ops unless a caller installed events.
+enum ProfKind { kProfForward = 0, kProfBackwardGauss = 1, kProfBackwardVoxel = 2 };
+void profile_mark(int kind, bool stop, cudaStream_t stream);
+
+// 2^x on the special-function unit (MUFU.EX2), flush-to-zero.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ unsigned lane_id() {
+    unsigned l;
+    asm("mov.u32 %0, %%laneid;" : "=r"(l));
+    return l;
+}
+
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+    const unsigned lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= (unsigned)o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ long long warp_inclusive_scan_ll(long long v) {
+    const unsigned lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        long long t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= (unsigned)o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ void red_add(float *p, float v) { atomicAdd(p, v); }
+__device__ __forceinline__ void red_add2(float *p, float a, float b) {
+    atomicAdd(reinterpret_cast<float2 *>(p), make_float2(a, b));
+}
+__device__ __forceinline__ void red_add4(float *p, float a, float b, float c,
+                                         float d) {
+    atomicAdd(reinterpret_cast<float4 *>(p), make_float4(a, b, c, d));
+}
+
+}  // namespace gsv

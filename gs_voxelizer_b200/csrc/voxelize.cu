@@ -1,0 +1,791 @@
+// Forward and backward voxelization of 3D Gaussians on 8x8x8 voxel tiles.
+//
+// Semantics follow gs_voxelizer/cuda/voxelize.cu of the reference:
+//   forward  :39-164   vol[v] = sum_g I_g * exp(sigma_g(v)) over the tile's
+//                      Gaussians, sigma = -1/2 d^T Q d, d = mu - (voxel+0.5),
+//                      skipping sigma > 0 / non-finite and alpha*mean(I)<1e-6
+//   backward :170-366 (per voxel) and :368-574 (per Gaussian): gradients of
+//                      the same sum w.r.t. mu, the six conic entries and I.
+//
+// The arithmetic is reorganised for the SM's issue rate (one warp
+// instruction per SMSP per clock, MUFU.EX2 at 16/clk/SM):
+//   * A per-Gaussian record is built once per call: centre, the conic scaled
+//     by log2(e) so that one ex2 gives exp(sigma), and the alpha*mean(I)
+//     cull rewritten as a threshold on the log2 exponent (s >= thr).
+//   * sigma restricted to a line of 8 voxels along z is a quadratic
+//     P + L*dz + C*dz^2; P and L are formed once per (Gaussian, column), so an
+//     evaluation costs 2-3 FP32 instructions, two compares and one ex2.
+//   * Backward sums are factored: along a z column only sum(w), sum(w dz) and
+//     sum(w dz^2) are accumulated (w = alpha * dL/dvol); the six conic and
+//     three position sums are rebuilt from them with the column's dx, dy.
+#include "common.cuh"
+
+namespace gsv {
+
+cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
+                                long long *partials, int *tile_bins,
+                                cudaStream_t stream);
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int C>
+struct Rec {
+    static constexpr int kF4 = C <= 2 ? 3 : 4;  // float4 per record
+};
+
+// record: r0 = (mx, my, mz, thr), r1 = (A, B, Cz, D), r2 = (E, F, I0, I1),
+//         r3 = (I2, I3, 0, 0)  with
+// s = A dx^2 + B dy^2 + Cz dz^2 + D dx dy + E dx dz + F dy dz = log2(e) sigma
+template <int C>
+__global__ void __launch_bounds__(256)
+prep_records_kernel(int n, const float4 *__restrict__ pos_radii,
+                    const float2 *__restrict__ conics,
+                    const float *__restrict__ intensities,
+                    float4 *__restrict__ rec) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    constexpr int R = Rec<C>::kF4;
+    const float4 p = pos_radii[i];
+    const float2 ab = conics[3 * i + 0], cd = conics[3 * i + 1],
+                 ef = conics[3 * i + 2];
+    float I[4] = {0.f, 0.f, 0.f, 0.f};
+    float mean = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        I[c] = intensities[i * C + c];
+        mean += I[c];
+    }
+    mean /= C;
+    float thr;
+    if (mean > 0.f) {
+        thr = (float)log2((double)0.000001f / (double)mean);
+    } else if (mean <= 0.f) {
+        thr = __int_as_float(0x7f800000);  // +inf: never contributes
+    } else {
+        thr = __int_as_float(0xff800000);  // NaN mean: -inf, output is NaN
+    }
+    const float h = -0.5f * kLog2e;
+    rec[i * R + 0] = make_float4(p.x, p.y, p.z, thr);
+    rec[i * R + 1] =
+        make_float4(h * ab.x, h * cd.y, h * ef.y, -kLog2e * ab.y);
+    rec[i * R + 2] = make_float4(-kLog2e * cd.x, -kLog2e * ef.x, I[0], I[1]);
+    if (R == 4) rec[i * R + 3] = make_float4(I[2], I[3], 0.f, 0.f);
+}
+
+__device__ __forceinline__ void tile_coords(const Geom &g, long long tile,
+                                            int &ox, int &oy, int &oz) {
+    const int tx = (int)(tile % g.Tx);
+    const long long rest = tile / g.Tx;
+    const int ty = (int)(rest % g.Ty);
+    const int tz = (int)(rest / g.Ty) + g.tz0;
+    ox = tx * kTile;
+    oy = ty * kTile;
+    oz = tz * kTile;
+}
+
+// ---------------------------------------------------------------- forward
+
+constexpr int kFwdThreads = 64;  // one thread per (x, y) column of a tile
+constexpr int kFwdBatch = 128;   // Gaussian records staged per pass
+
+template <int C>
+__global__ void __launch_bounds__(kFwdThreads, C <= 2 ? 16 : 8)
+vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
+               const int *__restrict__ ids, const float4 *__restrict__ rec,
+               float *__restrict__ out) {
+    constexpr int R = Rec<C>::kF4;
+    constexpr int kStage = (kFwdBatch * R * 4 > kTileVoxels * C)
+                               ? kFwdBatch * R * 4
+                               : kTileVoxels * C;
+    __shared__ __align__(16) float smem[kStage];
+    float4 *sb = reinterpret_cast<float4 *>(smem);
+
+    const long long tile = blockIdx.x;
+    int ox, oy, oz;
+    tile_coords(g, tile, ox, oy, oz);
+    const int lx = threadIdx.x & 7, ly = threadIdx.x >> 3;
+    const float fx = lx + 0.5f, fy = ly + 0.5f;
+
+    float acc[8][C];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < C; ++c) acc[j][c] = 0.f;
+
+    const int2 range = bins[tile];
+    for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
+        const int nb = min(kFwdBatch, range.y - s0);
+        __syncthreads();
+        for (int k = threadIdx.x; k < nb; k += kFwdThreads) {
+            const int gid = ids[s0 + k];
+            float4 r0 = rec[(size_t)gid * R];
+            r0.x -= (float)ox;
+            r0.y -= (float)oy;
+            r0.z -= (float)oz;
+            sb[k * R] = r0;
+#pragma unroll
+            for (int q = 1; q < R; ++q) sb[k * R + q] = rec[(size_t)gid * R + q];
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nb; ++t) {
+            const float4 r0 = sb[t * R + 0];
+            const float4 r1 = sb[t * R + 1];
+            const float4 r2 = sb[t * R + 2];
+            float I[C];
+            I[0] = r2.z;
+            if (C > 1) I[1 % C] = r2.w;
+            if (C > 2) {
+                const float4 r3 = sb[t * R + 3];
+                I[2 % C] = r3.x;
+                if (C > 3) I[3 % C] = r3.y;
+            }
+            const float dx = r0.x - fx, dy = r0.y - fy;
+            const float P = fmaf(dx, fmaf(r1.x, dx, r1.w * dy), r1.y * dy * dy);
+            const float L = fmaf(r2.x, dx, r2.y * dy);
+            const float thr = r0.w;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float dz = r0.z - ((float)j + 0.5f);
+                const float s = fmaf(dz, fmaf(r1.z, dz, L), P);
+                const bool ok = (s <= 0.f) & (s >= thr);
+                const float a = ex2(s);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    acc[j][c] = ok ? fmaf(I[c], a, acc[j][c]) : acc[j][c];
+            }
+        }
+    }
+
+    // stage the 8x8x8xC block and store it row by row (x fastest)
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+            smem[((j * 64) + ly * 8 + lx) * C + c] = acc[j][c];
+    __syncthreads();
+    {
+        const int row = threadIdx.x;  // 64 rows = 8 z * 8 y
+        const int z = oz + (row >> 3), y = oy + (row & 7);
+        if (z < g.z_end() && y < g.Y) {
+            const int nx = min(kTile, g.X - ox);
+            const size_t base =
+                (((size_t)(z - g.z_begin()) * g.Y + y) * g.X + ox) * C;
+            const float *src = smem + row * 8 * C;
+            float *dst = out + base;
+            if (nx == kTile && ((base & 3) == 0) &&
+                ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+                for (int q = 0; q < 2 * C; ++q)
+                    reinterpret_cast<float4 *>(dst)[q] =
+                        reinterpret_cast<const float4 *>(src)[q];
+            } else {
+                for (int q = 0; q < nx * C; ++q) dst[q] = src[q];
+            }
+        }
+    }
+}
+
+// --------------------------------------------------- backward (per Gaussian)
+//
+// Work item = (tile, bucket of up to 32 consecutive Gaussians of the tile's
+// sorted list). A warp takes one item at a time from a global counter. When a
+// bucket has m <= 16 Gaussians the warp splits the tile's 8 y-rows into
+// r = 2, 4 or 8 groups and gives each lane one (Gaussian, row group), so lanes
+// stay busy; the group partials are summed with shuffles before the atomics.
+// The tile's dL/dvol block is staged in the warp's shared memory as
+// [y][x][z][c] (z contiguous, row stride padded so that the r row groups hit
+// different banks).
+
+constexpr int kBwdWarps = 4;
+
+template <int C>
+struct BwdSmem {
+    static constexpr int kCol = 8 * C;              // floats per (y, x) column
+    static constexpr int kRow = 8 * kCol + 4;       // floats per y row (+pad)
+    static constexpr int kWarp = 8 * kRow;          // floats per warp buffer
+};
+
+template <int C>
+__device__ __forceinline__ void stage_grad_tile(const Geom &g,
+                                                const float *__restrict__ grad,
+                                                int ox, int oy, int oz,
+                                                float *buf, int lane) {
+    using S = BwdSmem<C>;
+    // 64 (z, y) rows of 8*C floats; lane handles rows lane and lane + 32
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = lane + 32 * h;
+        const int zl = row >> 3, yl = row & 7;
+        const int z = oz + zl, y = oy + yl;
+        float v[8 * C];
+        const bool row_in = (z < g.z_end()) && (y < g.Y);
+        const int nx = row_in ? min(kTile, g.X - ox) : 0;
+        const size_t base =
+            row_in ? (((size_t)(z - g.z_begin()) * g.Y + y) * g.X + ox) * C : 0;
+        if (nx == kTile && (base & 3) == 0 &&
+            ((reinterpret_cast<uintptr_t>(grad) & 15) == 0)) {
+#pragma unroll
+            for (int q = 0; q < 2 * C; ++q) {
+                const float4 t =
+                    __ldg(reinterpret_cast<const float4 *>(grad + base) + q);
+                v[4 * q + 0] = t.x;
+                v[4 * q + 1] = t.y;
+                v[4 * q + 2] = t.z;
+                v[4 * q + 3] = t.w;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8 * C; ++q)
+                v[q] = (q < nx * C) ? __ldg(grad + base + q) : 0.f;
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
+    }
+}
+
+template <int C>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
+                     const int *__restrict__ ids,
+                     const float4 *__restrict__ rec,
+                     const float2 *__restrict__ conics,
+                     const float *__restrict__ grad,
+                     const int2 *__restrict__ item_bins,
+                     const int *__restrict__ item_tile,
+                     const long long *__restrict__ item_total,
+                     int *__restrict__ work_counter,
+                     float *__restrict__ pos_grad,
+                     float *__restrict__ conic_grad,
+                     float *__restrict__ int_grad) {
+    using S = BwdSmem<C>;
+    constexpr int R = Rec<C>::kF4;
+    __shared__ __align__(16) float smem[kBwdWarps * S::kWarp];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float *buf = smem + wid * S::kWarp;
+    const int total = (int)*item_total;
+
+    while (true) {
+        int item = 0;
+        if (lane == 0) item = atomicAdd(work_counter, 1);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= total) break;
+
+        const int tile = item_tile[item];
+        const int2 range = bins[tile];
+        const int bucket = item - item_bins[tile].x;
+        const int start = range.x + 32 * bucket;
+        const int m = min(32, range.y - start);
+        int r = 1;
+        while (r < 8 && m * r * 2 <= 32) r <<= 1;
+        const int gs = 32 / r;           // lanes per row group
+        const int gi = lane % gs;        // Gaussian slot
+        const int sub = lane / gs;       // row group
+        const int rows = 8 / r;
+        const bool valid = gi < m;
+
+        int ox, oy, oz;
+        tile_coords(g, tile, ox, oy, oz);
+        __syncwarp();
+        stage_grad_tile<C>(g, grad, ox, oy, oz, buf, lane);
+        __syncwarp();
+
+        int gid = 0;
+        float4 r0 = make_float4(0.f, 0.f, 0.f, __int_as_float(0x7f800000));
+        float4 r1 = make_float4(0.f, 0.f, 0.f, 0.f), r2 = r1, r3 = r1;
+        if (valid) {
+            gid = ids[start + gi];
+            r0 = rec[(size_t)gid * R + 0];
+            r1 = rec[(size_t)gid * R + 1];
+            r2 = rec[(size_t)gid * R + 2];
+            if (R == 4) r3 = rec[(size_t)gid * R + 3];
+            r0.x -= (float)ox;
+            r0.y -= (float)oy;
+            r0.z -= (float)oz;
+        }
+        float I[C];
+        I[0] = r2.z;
+        if (C > 1) I[1 % C] = r2.w;
+        if (C > 2) I[2 % C] = r3.x;
+        if (C > 3) I[3 % C] = r3.y;
+        const float thr = r0.w;
+        float dz[8], cdz[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            dz[j] = r0.z - ((float)j + 0.5f);
+            cdz[j] = r1.z * dz[j];
+        }
+
+        // sums over the Gaussian's voxels of w-weighted monomials of d, where
+        // w = alpha * h and h = sum_c I_c dL/dvol_c (C > 1) or dL/dvol (C = 1)
+        float Sxx = 0.f, Syy = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f, Syz = 0.f;
+        float Vx = 0.f, Vy = 0.f, Vz = 0.f;
+        float W[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) W[c] = 0.f;
+
+#pragma unroll 1
+        for (int q = 0; q < rows; ++q) {
+            const int yl = sub * rows + q;
+            const float dy = r0.y - ((float)yl + 0.5f);
+            const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
+            float R0 = 0.f, R1 = 0.f, R2 = 0.f, Rx0 = 0.f, Rxx = 0.f, Rx1 = 0.f;
+            const float *colbase = buf + yl * S::kRow;
+#pragma unroll
+            for (int x = 0; x < 8; ++x) {
+                const float dx = r0.x - ((float)x + 0.5f);
+                const float P = fmaf(dx, fmaf(r1.x, dx, Dy), By2);
+                const float L = fmaf(r2.x, dx, Fy);
+                float gv[8 * C];
+#pragma unroll
+                for (int q4 = 0; q4 < 2 * C; ++q4) {
+                    const float4 t = reinterpret_cast<const float4 *>(
+                        colbase + x * S::kCol)[q4];
+                    gv[4 * q4 + 0] = t.x;
+                    gv[4 * q4 + 1] = t.y;
+                    gv[4 * q4 + 2] = t.z;
+                    gv[4 * q4 + 3] = t.w;
+                }
+                float T0 = 0.f, T1 = 0.f, T2 = 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float s = fmaf(dz[j], cdz[j] + L, P);
+                    const bool ok = (s <= 0.f) & (s >= thr);
+                    const float a = ok ? ex2(s) : 0.f;
+                    float w;
+                    if (C == 1) {
+                        w = a * gv[j];  // intensity grad = sum(w) = sum(R0)
+                    } else {
+                        float h = I[0] * gv[j * C];
+#pragma unroll
+                        for (int c = 1; c < C; ++c)
+                            h = fmaf(I[c], gv[j * C + c], h);
+#pragma unroll
+                        for (int c = 0; c < C; ++c)
+                            W[c] = fmaf(a, gv[j * C + c], W[c]);
+                        w = a * h;
+                    }
+                    T0 += w;
+                    const float t = w * dz[j];
+                    T1 += t;
+                    T2 = fmaf(t, dz[j], T2);
+                }
+                R0 += T0;
+                R1 += T1;
+                R2 += T2;
+                const float u = dx * T0;
+                Rx0 += u;
+                Rxx = fmaf(u, dx, Rxx);
+                Rx1 = fmaf(dx, T1, Rx1);
+            }
+            if (C == 1) W[0] += R0;
+            Sxx += Rxx;
+            Szz += R2;
+            Sxz += Rx1;
+            Vx += Rx0;
+            Vz += R1;
+            Syy = fmaf(dy * dy, R0, Syy);
+            Sxy = fmaf(dy, Rx0, Sxy);
+            Syz = fmaf(dy, R1, Syz);
+            Vy = fmaf(dy, R0, Vy);
+        }
+
+        // combine row groups (lanes gi, gi+gs, gi+2gs, ...)
+        for (int o = gs; o < 32; o <<= 1) {
+            Sxx += __shfl_xor_sync(0xffffffffu, Sxx, o);
+            Syy += __shfl_xor_sync(0xffffffffu, Syy, o);
+            Szz += __shfl_xor_sync(0xffffffffu, Szz, o);
+            Sxy += __shfl_xor_sync(0xffffffffu, Sxy, o);
+            Sxz += __shfl_xor_sync(0xffffffffu, Sxz, o);
+            Syz += __shfl_xor_sync(0xffffffffu, Syz, o);
+            Vx += __shfl_xor_sync(0xffffffffu, Vx, o);
+            Vy += __shfl_xor_sync(0xffffffffu, Vy, o);
+            Vz += __shfl_xor_sync(0xffffffffu, Vz, o);
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                W[c] += __shfl_xor_sync(0xffffffffu, W[c], o);
+        }
+
+        if (valid && sub == 0) {
+            const float k = (C == 1) ? I[0] : 1.f;  // sigma_grad = I * w (C=1)
+            const float2 ab = conics[3 * gid + 0], cd = conics[3 * gid + 1],
+                         ef = conics[3 * gid + 2];
+            const float a_ = ab.x, b_ = ab.y, c_ = cd.x, d_ = cd.y, e_ = ef.x,
+                        f_ = ef.y;
+            const float vx = k * Vx, vy = k * Vy, vz = k * Vz;
+            red_add4(pos_grad + 4 * (size_t)gid,
+                     -(a_ * vx + b_ * vy + c_ * vz),
+                     -(b_ * vx + d_ * vy + e_ * vz),
+                     -(c_ * vx + e_ * vy + f_ * vz), 0.f);
+            float *cg = conic_grad + 6 * (size_t)gid;
+            red_add2(cg + 0, -0.5f * k * Sxx, -k * Sxy);
+            red_add2(cg + 2, -k * Sxz, -0.5f * k * Syy);
+            red_add2(cg + 4, -k * Syz, -0.5f * k * Szz);
+            float *ig = int_grad + (size_t)C * gid;
+            if (C == 4) {
+                red_add4(ig, W[0], W[C > 1 ? 1 : 0], W[C > 2 ? 2 : 0],
+                         W[C > 3 ? 3 : 0]);
+            } else if (C == 2) {
+                red_add2(ig, W[0], W[C > 1 ? 1 : 0]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < C; ++c) red_add(ig + c, W[c]);
+            }
+        }
+    }
+}
+
+// Per-tile item counts (ceil(n_t / 32)) for the planner.
+__global__ void __launch_bounds__(256)
+item_count_kernel(const int2 *__restrict__ bins, long long ntiles,
+                  int *__restrict__ counts) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= ntiles) return;
+    const int2 r = bins[t];
+    const int n = max(0, r.y - r.x);
+    counts[t] = (n + 31) / 32;
+}
+
+__global__ void __launch_bounds__(256)
+item_fill_kernel(const int2 *__restrict__ item_bins, long long ntiles,
+                 int *__restrict__ item_tile) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= ntiles) return;
+    const int2 r = item_bins[t];
+    for (int k = r.x; k < r.y; ++k) item_tile[k] = (int)t;
+}
+
+// ------------------------------------------------------ backward (per voxel)
+//
+// Voxel-centric variant (the reference's use_per_gaussian_backward=False):
+// the forward's CTA layout, one thread per (x, y) column of 8 voxels; each
+// thread folds its column into the per-Gaussian sums, the warp reduces them,
+// and lane 0 issues one set of vector atomics per warp and Gaussian.
+
+template <int C>
+__global__ void __launch_bounds__(kFwdThreads, C <= 2 ? 16 : 8)
+vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
+                     const int *__restrict__ ids,
+                     const float4 *__restrict__ rec,
+                     const float2 *__restrict__ conics,
+                     const float *__restrict__ grad,
+                     float *__restrict__ pos_grad,
+                     float *__restrict__ conic_grad,
+                     float *__restrict__ int_grad) {
+    constexpr int R = Rec<C>::kF4;
+    __shared__ __align__(16) float4 sb[kFwdBatch * R];
+    __shared__ int sid[kFwdBatch];
+
+    const long long tile = blockIdx.x;
+    int ox, oy, oz;
+    tile_coords(g, tile, ox, oy, oz);
+    const int lane = threadIdx.x & 31;
+    const int lx = threadIdx.x & 7, ly = threadIdx.x >> 3;
+    const float fx = lx + 0.5f, fy = ly + 0.5f;
+
+    // this thread's column of dL/dvol (zero outside the volume)
+    float gv[8][C];
+    {
+        const int x = ox + lx, y = oy + ly;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int z = oz + j;
+            const bool in = x < g.X && y < g.Y && z < g.z_end();
+            const size_t base =
+                in ? (((size_t)(z - g.z_begin()) * g.Y + y) * g.X + x) * C : 0;
+#pragma unroll
+            for (int c = 0; c < C; ++c) gv[j][c] = in ? grad[base + c] : 0.f;
+        }
+    }
+
+    const int2 range = bins[tile];
+    for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
+        const int nb = min(kFwdBatch, range.y - s0);
+        __syncthreads();
+        for (int k = threadIdx.x; k < nb; k += kFwdThreads) {
+            const int gid = ids[s0 + k];
+            sid[k] = gid;
+            float4 r0 = rec[(size_t)gid * R];
+            r0.x -= (float)ox;
+            r0.y -= (float)oy;
+            r0.z -= (float)oz;
+            sb[k * R] = r0;
+#pragma unroll
+            for (int q = 1; q < R; ++q) sb[k * R + q] = rec[(size_t)gid * R + q];
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nb; ++t) {
+            const float4 r0 = sb[t * R + 0];
+            const float4 r1 = sb[t * R + 1];
+            const float4 r2 = sb[t * R + 2];
+            float I[C];
+            I[0] = r2.z;
+            if (C > 1) I[1 % C] = r2.w;
+            if (C > 2) {
+                const float4 r3 = sb[t * R + 3];
+                I[2 % C] = r3.x;
+                if (C > 3) I[3 % C] = r3.y;
+            }
+            const float dx = r0.x - fx, dy = r0.y - fy;
+            const float P = fmaf(dx, fmaf(r1.x, dx, r1.w * dy), r1.y * dy * dy);
+            const float L = fmaf(r2.x, dx, r2.y * dy);
+            const float thr = r0.w;
+            float T0 = 0.f, T1 = 0.f, T2 = 0.f;
+            float W[C];
+#pragma unroll
+            for (int c = 0; c < C; ++c) W[c] = 0.f;
+            bool touched = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float dz = r0.z - ((float)j + 0.5f);
+                const float s = fmaf(dz, fmaf(r1.z, dz, L), P);
+                const bool ok = (s <= 0.f) & (s >= thr);
+                const float a = ok ? ex2(s) : 0.f;
+                float h = I[0] * gv[j][0];
+#pragma unroll
+                for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[j][c], h);
+#pragma unroll
+                for (int c = 0; c < C; ++c) W[c] = fmaf(a, gv[j][c], W[c]);
+                const float w = a * h;
+                touched |= (a != 0.f);
+                T0 += w;
+                const float tt = w * dz;
+                T1 += tt;
+                T2 = fmaf(tt, dz, T2);
+            }
+            if (!__any_sync(0xffffffffu, touched)) continue;
+            float v[9 + C];
+            v[0] = dx * dx * T0;  // Sxx
+            v[1] = dy * dy * T0;  // Syy
+            v[2] = T2;            // Szz
+            v[3] = dx * dy * T0;  // Sxy
+            v[4] = dx * T1;       // Sxz
+            v[5] = dy * T1;       // Syz
+            v[6] = dx * T0;       // Vx
+            v[7] = dy * T0;       // Vy
+            v[8] = T1;            // Vz
+#pragma unroll
+            for (int c = 0; c < C; ++c) v[9 + c] = W[c];
+#pragma unroll
+            for (int k = 0; k < 9 + C; ++k)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                    v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
+            if (lane == 0) {
+                const int gid = sid[t];
+                const float2 ab = conics[3 * gid + 0],
+                             cd = conics[3 * gid + 1],
+                             ef = conics[3 * gid + 2];
+                red_add4(pos_grad + 4 * (size_t)gid,
+                         -(ab.x * v[6] + ab.y * v[7] + cd.x * v[8]),
+                         -(ab.y * v[6] + cd.y * v[7] + ef.x * v[8]),
+                         -(cd.x * v[6] + ef.x * v[7] + ef.y * v[8]), 0.f);
+                float *cg = conic_grad + 6 * (size_t)gid;
+                red_add2(cg + 0, -0.5f * v[0], -v[3]);
+                red_add2(cg + 2, -v[4], -0.5f * v[1]);
+                red_add2(cg + 4, -v[5], -0.5f * v[2]);
+                float *ig = int_grad + (size_t)C * gid;
+#pragma unroll
+                for (int c = 0; c < C; ++c) red_add(ig + c, v[9 + c]);
+            }
+        }
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ host launchers
+
+struct VoxLayout {
+    size_t rec, item_counts, item_bins, partials, item_tile, counter, total;
+};
+
+static inline size_t align256v(size_t x) { return (x + 255) & ~size_t(255); }
+
+VoxLayout vox_layout(long long n, int channels, long long ntiles,
+                     long long nisect) {
+    VoxLayout L;
+    const int R = channels <= 2 ? 3 : 4;
+    const long long nblocks = (ntiles + 4095) / 4096;
+    const long long max_items = (nisect + 31) / 32 + ntiles;
+    size_t off = 0;
+    L.rec = off;
+    off = align256v(off + sizeof(float4) * (size_t)R * (size_t)(n > 0 ? n : 1));
+    L.item_counts = off;
+    off = align256v(off + sizeof(int) * (size_t)ntiles);
+    L.item_bins = off;
+    off = align256v(off + sizeof(int2) * (size_t)ntiles);
+    L.partials = off;
+    off = align256v(off + sizeof(long long) * (size_t)(nblocks + 1));
+    L.item_tile = off;
+    off = align256v(off + sizeof(int) * (size_t)(max_items + 1));
+    L.counter = off;
+    off = align256v(off + sizeof(int) * 4);
+    L.total = off;
+    return L;
+}
+
+size_t vox_workspace_bytes(long long n, int channels, long long ntiles,
+                           long long nisect) {
+    return vox_layout(n, channels, ntiles, nisect).total;
+}
+
+static cudaError_t launch_prep(int n, int C, const float *pos_radii,
+                               const float *conics, const float *intens,
+                               float4 *rec, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    const int blocks = (n + 255) / 256;
+    const float4 *p = reinterpret_cast<const float4 *>(pos_radii);
+    const float2 *q = reinterpret_cast<const float2 *>(conics);
+    switch (C) {
+        case 1: prep_records_kernel<1><<<blocks, 256, 0, stream>>>(n, p, q, intens, rec); break;
+        case 2: prep_records_kernel<2><<<blocks, 256, 0, stream>>>(n, p, q, intens, rec); break;
+        case 3: prep_records_kernel<3><<<blocks, 256, 0, stream>>>(n, p, q, intens, rec); break;
+        case 4: prep_records_kernel<4><<<blocks, 256, 0, stream>>>(n, p, q, intens, rec); break;
+        default: return cudaErrorInvalidValue;
+    }
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
+                               const int *tile_bins, const float *pos_radii,
+                               const float *conics, const float *intens,
+                               float *out, void *ws, cudaStream_t stream) {
+    const long long ntiles = g.slab_tiles();
+    const VoxLayout L = vox_layout(n, C, ntiles, 0);
+    float4 *rec = reinterpret_cast<float4 *>(static_cast<char *>(ws) + L.rec);
+    cudaError_t err = launch_prep(n, C, pos_radii, conics, intens, rec, stream);
+    if (err) return err;
+    if (ntiles == 0) return cudaSuccess;
+    const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
+    const unsigned grid = (unsigned)ntiles;
+    profile_mark(kProfForward, false, stream);
+    switch (C) {
+        case 1: vox_fwd_kernel<1><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
+        case 2: vox_fwd_kernel<2><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
+        case 3: vox_fwd_kernel<3><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
+        case 4: vox_fwd_kernel<4><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
+        default: return cudaErrorInvalidValue;
+    }
+    profile_mark(kProfForward, true, stream);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+template <int C>
+static int bwd_gauss_grid() {
+    static int cached = 0;
+    if (cached) return cached;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, vox_bwd_gauss_kernel<C>, kBwdWarps * 32, 0);
+    int dev = 0, sms = kSMs;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cached = std::max(1, per_sm) * sms;
+    return cached;
+}
+
+cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
+                                      long long nisect, const int *ids,
+                                      const int *tile_bins,
+                                      const float *pos_radii,
+                                      const float *conics,
+                                      const float *intens, const float *grad,
+                                      float *pos_grad, float *conic_grad,
+                                      float *int_grad, void *ws,
+                                      cudaStream_t stream) {
+    const long long ntiles = g.slab_tiles();
+    const VoxLayout L = vox_layout(n, C, ntiles, nisect);
+    char *base = static_cast<char *>(ws);
+    float4 *rec = reinterpret_cast<float4 *>(base + L.rec);
+    int *item_counts = reinterpret_cast<int *>(base + L.item_counts);
+    int *item_bins = reinterpret_cast<int *>(base + L.item_bins);
+    long long *partials = reinterpret_cast<long long *>(base + L.partials);
+    int *item_tile = reinterpret_cast<int *>(base + L.item_tile);
+    int *counter = reinterpret_cast<int *>(base + L.counter);
+    const long long nblocks = (ntiles + 4095) / 4096;
+
+    cudaError_t err;
+    if ((err = cudaMemsetAsync(pos_grad, 0, sizeof(float) * 4 * (size_t)n, stream))) return err;
+    if ((err = cudaMemsetAsync(conic_grad, 0, sizeof(float) * 6 * (size_t)n, stream))) return err;
+    if ((err = cudaMemsetAsync(int_grad, 0, sizeof(float) * C * (size_t)n, stream))) return err;
+    if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
+    if ((err = cudaMemsetAsync(counter, 0, sizeof(int) * 4, stream))) return err;
+    if ((err = launch_prep(n, C, pos_radii, conics, intens, rec, stream))) return err;
+
+    const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
+    const unsigned tblocks = (unsigned)((ntiles + 255) / 256);
+    item_count_kernel<<<tblocks, 256, 0, stream>>>(bins, ntiles, item_counts);
+    if ((err = scan_counts_to_bins(item_counts, ntiles, partials, item_bins, stream))) return err;
+    item_fill_kernel<<<tblocks, 256, 0, stream>>>(
+        reinterpret_cast<const int2 *>(item_bins), ntiles, item_tile);
+    const long long *total = partials + nblocks;
+    const float2 *cq = reinterpret_cast<const float2 *>(conics);
+    const int2 *ib = reinterpret_cast<const int2 *>(item_bins);
+#define GSV_BWD(Cc)                                                          \
+    vox_bwd_gauss_kernel<Cc><<<bwd_gauss_grid<Cc>(), kBwdWarps * 32, 0,      \
+                               stream>>>(g, bins, ids, rec, cq, grad, ib,    \
+                                         item_tile, total, counter,          \
+                                         pos_grad, conic_grad, int_grad)
+    profile_mark(kProfBackwardGauss, false, stream);
+    switch (C) {
+        case 1: GSV_BWD(1); break;
+        case 2: GSV_BWD(2); break;
+        case 3: GSV_BWD(3); break;
+        case 4: GSV_BWD(4); break;
+        default: return cudaErrorInvalidValue;
+    }
+    profile_mark(kProfBackwardGauss, true, stream);
+#undef GSV_BWD
+    count_launches(3);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_vox_backward_voxel(const Geom &g, int C, int n,
+                                      long long nisect, const int *ids,
+                                      const int *tile_bins,
+                                      const float *pos_radii,
+                                      const float *conics,
+                                      const float *intens, const float *grad,
+                                      float *pos_grad, float *conic_grad,
+                                      float *int_grad, void *ws,
+                                      cudaStream_t stream) {
+    const long long ntiles = g.slab_tiles();
+    const VoxLayout L = vox_layout(n, C, ntiles, nisect);
+    float4 *rec = reinterpret_cast<float4 *>(static_cast<char *>(ws) + L.rec);
+    cudaError_t err;
+    if ((err = cudaMemsetAsync(pos_grad, 0, sizeof(float) * 4 * (size_t)n, stream))) return err;
+    if ((err = cudaMemsetAsync(conic_grad, 0, sizeof(float) * 6 * (size_t)n, stream))) return err;
+    if ((err = cudaMemsetAsync(int_grad, 0, sizeof(float) * C * (size_t)n, stream))) return err;
+    if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
+    if ((err = launch_prep(n, C, pos_radii, conics, intens, rec, stream))) return err;
+    const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
+    const float2 *cq = reinterpret_cast<const float2 *>(conics);
+    const unsigned grid = (unsigned)ntiles;
+#define GSV_BWDV(Cc)                                                         \
+    vox_bwd_voxel_kernel<Cc><<<grid, kFwdThreads, 0, stream>>>(              \
+        g, bins, ids, rec, cq, grad, pos_grad, conic_grad, int_grad)
+    profile_mark(kProfBackwardVoxel, false, stream);
+    switch (C) {
+        case 1: GSV_BWDV(1); break;
+        case 2: GSV_BWDV(2); break;
+        case 3: GSV_BWDV(3); break;
+        case 4: GSV_BWDV(4); break;
+        default: return cudaErrorInvalidValue;
+    }
+    profile_mark(kProfBackwardVoxel, true, stream);
+#undef GSV_BWDV
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace gsv

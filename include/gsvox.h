@@ -1,0 +1,238 @@
+/*
+ * gsvox.h - C ABI of the B200-native Gaussian voxelization path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as `void*`; NULL = legacy default stream) and returns a status
+ * code (GSV_OK on success). Nothing here allocates device memory: callers
+ * pass output buffers and, where a function needs scratch space, a
+ * workspace whose size they query first with the matching
+ * `*_workspace_bytes` function. All launches are asynchronous on `stream`.
+ *
+ * Conventions shared with the reference (PaPieta/gs-voxelizer):
+ *   - Volume sizes are given as (z, y, x) = (depth, height, width), the
+ *     order of the reference's Python tuples.
+ *   - Tiles are 8x8x8 voxels; tile id = tz*Ty*Tx + ty*Tx + tx with
+ *     Tx = ceil(X/8), Ty = ceil(Y/8), Tz = ceil(Z/8).
+ *   - pos3d_radii is [N,4] float (voxel-space x, y, z, radius), conics is
+ *     [N,6] float (inverse covariance a,b,c,d,e,f = Q00,Q01,Q02,Q11,Q12,Q22),
+ *     tile_min / tile_max are [N,3] int32 (x,y,z), intensities [N,C] float,
+ *     the volume is [Z,Y,X,C] float.
+ *   - 1 <= C <= 4 channels.
+ *
+ * Each function names the reference interface it replaces (file:line in the
+ * reference project).
+ */
+#ifndef GSVOX_H
+#define GSVOX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GSV_API __attribute__((visibility("default")))
+#else
+#define GSV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gsv_status {
+    GSV_OK = 0,
+    GSV_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad dims   */
+    GSV_ERR_UNSUPPORTED_CHANNELS = 2, /* C outside 1..4                      */
+    GSV_ERR_WORKSPACE_TOO_SMALL = 3,
+    GSV_ERR_SIZE_OVERFLOW = 4,    /* sizes beyond the 32-bit index formats    */
+    GSV_ERR_CUDA = 5              /* a CUDA launch or runtime call failed     */
+};
+
+/* Human-readable text of the last error raised on the calling host thread. */
+GSV_API const char *gsv_last_error(void);
+
+/* Library version, e.g. "0.1.0". */
+GSV_API const char *gsv_version(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads). Instrumentation for benchmarks; no reference
+ * counterpart. */
+GSV_API uint64_t gsv_launch_count(void);
+
+/* Install CUDA events (cudaEvent_t, passed as void*) that later calls on this
+ * host thread record immediately before and after the main voxelization
+ * kernel of kind `which` (0 = forward, 1 = per-Gaussian backward,
+ * 2 = per-voxel backward), on the call's stream; NULL, NULL removes them.
+ * Instrumentation for benchmarks; no reference counterpart. */
+GSV_API int gsv_profile_kernel(int32_t which, void *start_event,
+                               void *stop_event);
+
+/*
+ * Projection forward: quaternion/scale -> voxel-space inverse covariance
+ * (conic), cull radius, 3D tile bounding box and tile count per Gaussian.
+ * Writes every output element (culled Gaussians get zeros).
+ * Replaces optim_to_render_forward_torch, gs_voxelizer/cuda/bindings.cu:44
+ * (kernel gs_voxelizer/cuda/optim_to_render.cu:48).
+ *   vol_size_voxel[3] = (Z, Y, X); vol_size_world[3], vol_center_pos[3] in
+ *   (z, y, x) order.
+ */
+GSV_API int gsv_optim_to_render_forward(
+    int32_t num_gaussians, int32_t channels,
+    const float *pos3d, const float *scale3d, const float *quat,
+    const float *intensities,
+    const int32_t vol_size_voxel[3], const float vol_size_world[3],
+    const float vol_center_pos[3],
+    float *pos3d_radii_out, float *conics_out,
+    int32_t *tile_min_out, int32_t *tile_max_out, int32_t *num_tiles_hit_out,
+    void *stream);
+
+/*
+ * Projection backward: conic / position gradients -> gradients of pos3d
+ * [N,3], scale3d [N,3] and quat [N,4]. Writes every output element.
+ * Replaces optim_to_render_backward_torch, gs_voxelizer/cuda/bindings.cu:201
+ * (kernel gs_voxelizer/cuda/optim_to_render.cu:246).
+ */
+GSV_API int gsv_optim_to_render_backward(
+    int32_t num_gaussians,
+    const float *pos3d, const float *scale3d, const float *quat,
+    const int32_t vol_size_voxel[3], const float vol_size_world[3],
+    const float vol_center_pos[3],
+    const float *pos3d_radii_grad_in, const float *conics_grad_in,
+    const float *pos3d_radii_out,
+    float *pos3d_grad_out, float *scale3d_grad_out, float *quat_grad_out,
+    void *stream);
+
+/*
+ * Binning: expand each Gaussian's tile box into (tile, gaussian) pairs and
+ * order them by tile id, then by gaussian id (the order of the reference's
+ * stable radix sort), and write the per-tile [start, end) ranges. Tiles that
+ * no Gaussian touches get (0, 0), as in the reference.
+ * gaussian_ids_sorted_out holds num_intersects int32, tile_bins_out holds
+ * 2*T int32. cum_tiles_hit (inclusive prefix sum of num_tiles_hit) is
+ * accepted for interface parity; the result depends only on the tile boxes.
+ * Replaces bin_and_sort_gaussians_torch, gs_voxelizer/cuda/bindings.cu:261
+ * (kernels gs_voxelizer/cuda/bin_and_sort_gaussians.cu:11,40 and the CUB sort
+ * at bindings.cu:316-345).
+ */
+GSV_API size_t gsv_bin_and_sort_workspace_bytes(
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t vol_size_voxel[3]);
+
+GSV_API int gsv_bin_and_sort_gaussians(
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *tile_min, const int32_t *tile_max,
+    const int32_t *cum_tiles_hit,
+    const int32_t vol_size_voxel[3],
+    int32_t *gaussian_ids_sorted_out, int32_t *tile_bins_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Slab variant of the binning used by z-slab sharding: only tiles with
+ * tile_z_begin <= tz < tile_z_end are binned, and tile ids / tile_bins are
+ * local to the slab (tile id minus tile_z_begin*Ty*Tx). The result equals the
+ * full-volume binning restricted to the slab. num_intersects must be the
+ * number of (tile, gaussian) pairs that fall inside the slab.
+ * No single reference counterpart: extends bindings.cu:261 for sharding.
+ */
+GSV_API size_t gsv_bin_and_sort_slab_workspace_bytes(
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end);
+
+GSV_API int gsv_bin_and_sort_gaussians_slab(
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *tile_min, const int32_t *tile_max,
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
+    int32_t *gaussian_ids_sorted_out, int32_t *tile_bins_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Count the (tile, gaussian) pairs of a z-slab of tiles into *count_out
+ * (one int64 in device memory). No reference counterpart (sharding only).
+ */
+GSV_API int gsv_count_slab_intersects(
+    int32_t num_gaussians, const int32_t *tile_min, const int32_t *tile_max,
+    int32_t tile_z_begin, int32_t tile_z_end, int64_t *count_out,
+    void *stream);
+
+/*
+ * Forward voxelization: vol[z,y,x,c] = sum over the tile's Gaussians of
+ * I_c * exp(-1/2 d^T Q d), with the reference's two culls (sigma > 0 or not
+ * finite; alpha * mean(I) < 1e-6). out_vol holds Z*Y*X*C floats and is fully
+ * written.
+ * Replaces voxelize_forward_torch, gs_voxelizer/cuda/bindings.cu:362
+ * (kernel gs_voxelizer/cuda/voxelize.cu:39).
+ */
+GSV_API size_t gsv_voxelize_workspace_bytes(
+    int32_t num_gaussians, int32_t channels, int64_t num_intersects,
+    const int32_t vol_size_voxel[3]);
+
+GSV_API int gsv_voxelize_forward(
+    const int32_t vol_size_voxel[3], int32_t channels,
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    float *out_vol,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Backward voxelization, per-Gaussian work distribution (the reference's
+ * default): reads dL/dvol [Z,Y,X,C], writes pos3d_grad [N,4] (w = 0),
+ * conics_grad [N,6], intensities_grad [N,C]. Outputs are fully written.
+ * Replaces voxelize_backward_per_gaussian_torch, bindings.cu:589
+ * (kernel gs_voxelizer/cuda/voxelize.cu:368 and helpers :577-610).
+ */
+GSV_API int gsv_voxelize_backward_per_gaussian(
+    const int32_t vol_size_voxel[3], int32_t channels,
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    const float *vol_grad_in,
+    float *pos3d_grad_out, float *conics_grad_out, float *intensities_grad_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Backward voxelization, per-voxel work distribution (reference's
+ * use_per_gaussian_backward=False). Same outputs as above.
+ * Replaces voxelize_backward_torch, bindings.cu:462
+ * (kernel gs_voxelizer/cuda/voxelize.cu:170).
+ */
+GSV_API int gsv_voxelize_backward(
+    const int32_t vol_size_voxel[3], int32_t channels,
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    const float *vol_grad_in,
+    float *pos3d_grad_out, float *conics_grad_out, float *intensities_grad_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Slab variants of the voxelization used by z-slab sharding: the volume
+ * buffers cover only voxel z in [8*tile_z_begin, min(Z, 8*tile_z_end)),
+ * tile_bins comes from gsv_bin_and_sort_gaussians_slab, positions stay in
+ * full-volume voxel coordinates. No single reference counterpart.
+ */
+GSV_API size_t gsv_voxelize_slab_workspace_bytes(
+    int32_t num_gaussians, int32_t channels, int64_t num_intersects,
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end);
+
+GSV_API int gsv_voxelize_forward_slab(
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
+    int32_t channels, int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    float *out_vol,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+GSV_API int gsv_voxelize_backward_per_gaussian_slab(
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
+    int32_t channels, int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    const float *vol_grad_in,
+    float *pos3d_grad_out, float *conics_grad_out, float *intensities_grad_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSVOX_H */

@@ -1,0 +1,133 @@
+"""GPU parity against the reference's own CUDA extension (compiled from its
+unmodified sources for sm_100a by oracle/build_ref.py into oracle/_ref).
+
+Same inputs into both; integers must match bit for bit, floats within the
+stated tolerances (volume 1e-5 relative + 1e-6 absolute, gradients 1e-4
+relative + 1e-4 of the array's max, since atomic order differs)."""
+import numpy as np
+import pytest
+import torch
+
+from tests import _cases as K
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle import ref_api
+    if not ref_api.available():
+        pytest.skip("reference extension not built (oracle/_ref)")
+    return ref_api.ext()
+
+
+def C():
+    from gs_voxelizer_b200 import cuda as _C
+    return _C
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def grad_close(got, want, name):
+    got, want = host(got).astype(np.float64), host(want).astype(np.float64)
+    tol = 1e-4 * np.abs(want) + 1e-4 * max(np.abs(want).max(), 1e-30)
+    bad = np.abs(got - want) > tol
+    assert not bad.any(), f"{name}: {bad.sum()} of {bad.size} out of tolerance"
+
+
+CASES = [
+    dict(vol=(60, 50, 70), n=3000, channels=1, scale=(0.005, 0.05)),
+    dict(vol=(33, 40, 27), n=1500, channels=3, scale=(0.005, 0.06)),
+    dict(vol=(64, 64, 64), n=8000, channels=4, scale=(0.002, 0.03)),
+]
+
+
+def run_both(ref, cfg):
+    pos, scale, quat, inten = (dev(a) for a in K.inputs(cfg))
+    a = C().optim_to_render_forward(cfg.n, pos, scale, quat, inten, cfg.vol,
+                                    cfg.world, cfg.center)
+    b = ref.optim_to_render_forward(cfg.n, pos, scale, quat, inten, cfg.vol,
+                                    cfg.world, cfg.center)
+    torch.cuda.synchronize()
+    return (pos, scale, quat, inten), a, b
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_projection_bit_exact_against_reference(ref, case):
+    cfg = K.small_config(seed=41, **case)
+    _, a, b = run_both(ref, cfg)
+    for x, y, name in zip(a[2:], b[2:], ("tile_min", "tile_max", "num_tiles_hit")):
+        assert torch.equal(x, y), name
+    np.testing.assert_allclose(host(a[0]), host(b[0]), rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(host(a[1]), host(b[1]), rtol=1e-5,
+                               atol=1e-6 * float(b[1].abs().max()))
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_binning_and_voxelize_against_reference(ref, case):
+    cfg = K.small_config(seed=42, **case)
+    (pos, scale, quat, inten), a, b = run_both(ref, cfg)
+    pr, cq, tmin, tmax, nt = a
+    cum = torch.cumsum(nt, 0, dtype=torch.int32)
+    n_isect = int(cum[-1].item())
+    ids_a, bins_a = C().bin_and_sort_gaussians(cfg.n, n_isect, tmin, tmax, cum, cfg.vol)
+    ids_b, bins_b = ref.bin_and_sort_gaussians(cfg.n, n_isect, tmin, tmax, cum, cfg.vol)
+    torch.cuda.synchronize()
+    assert torch.equal(ids_a, ids_b)
+    assert torch.equal(bins_a, bins_b)
+
+    vol_a = C().voxelize_forward(cfg.vol, ids_a, bins_a, pr, cq, inten)
+    vol_b = ref.voxelize_forward(cfg.vol, ids_b, bins_b, pr, cq, inten)
+    va, vb = host(vol_a).astype(np.float64), host(vol_b).astype(np.float64)
+    bad = np.abs(va - vb) > 1e-5 * np.abs(vb) + 1e-6
+    assert not bad.any(), f"{bad.sum()} voxels differ, max {np.abs(va - vb).max():.2e}"
+
+    W = torch.randn(vol_a.shape, device="cuda",
+                    generator=torch.Generator("cuda").manual_seed(3))
+    ga = C().voxelize_backward_per_gaussian(cfg.vol, ids_a, bins_a, pr, cq, inten, W)
+    gb = ref.voxelize_backward_per_gaussian(cfg.vol, ids_b, bins_b, pr, cq, inten, W)
+    for x, y, name in zip(ga, gb, ("pos", "conic", "intensity")):
+        grad_close(x, y, name)
+    gv = C().voxelize_backward(cfg.vol, ids_a, bins_a, pr, cq, inten, W)
+    for x, y, name in zip(gv, gb, ("pos", "conic", "intensity")):
+        grad_close(x, y, "per-voxel " + name)
+
+    G = torch.randn((cfg.n, 6), device="cuda")
+    Gp = torch.randn((cfg.n, 4), device="cuda")
+    pa = C().optim_to_render_backward(cfg.n, pos, scale, quat, cfg.vol, cfg.world,
+                                      cfg.center, Gp, G, pr)
+    pb = ref.optim_to_render_backward(cfg.n, pos, scale, quat, cfg.vol, cfg.world,
+                                      cfg.center, Gp, G, pr)
+    for x, y, name in zip(pa, pb, ("pos3d", "scale3d", "quat")):
+        grad_close(x, y, name)
+
+
+def test_full_size_step256_against_reference(ref):
+    """BASELINE configuration 2 at full size through both implementations."""
+    from gs_voxelizer_b200.workloads import CONFIGS
+    cfg = CONFIGS["step256"]
+    (pos, scale, quat, inten), a, b = run_both(ref, cfg)
+    for x, y in zip(a[2:], b[2:]):
+        assert torch.equal(x, y)
+    pr, cq, tmin, tmax, nt = a
+    cum = torch.cumsum(nt, 0, dtype=torch.int32)
+    n_isect = int(cum[-1].item())
+    ids_a, bins_a = C().bin_and_sort_gaussians(cfg.n, n_isect, tmin, tmax, cum, cfg.vol)
+    ids_b, bins_b = ref.bin_and_sort_gaussians(cfg.n, n_isect, tmin, tmax, cum, cfg.vol)
+    assert torch.equal(ids_a, ids_b) and torch.equal(bins_a, bins_b)
+    vol_a = C().voxelize_forward(cfg.vol, ids_a, bins_a, pr, cq, inten)
+    vol_b = ref.voxelize_forward(cfg.vol, ids_b, bins_b, pr, cq, inten)
+    err = (vol_a.double() - vol_b.double()).abs()
+    assert bool((err <= 1e-5 * vol_b.double().abs() + 1e-6).all()), float(err.max())
+    W = torch.randn(vol_a.shape, device="cuda",
+                    generator=torch.Generator("cuda").manual_seed(4))
+    ga = C().voxelize_backward_per_gaussian(cfg.vol, ids_a, bins_a, pr, cq, inten, W)
+    gb = ref.voxelize_backward_per_gaussian(cfg.vol, ids_b, bins_b, pr, cq, inten, W)
+    for x, y, name in zip(ga, gb, ("pos", "conic", "intensity")):
+        grad_close(x, y, name)

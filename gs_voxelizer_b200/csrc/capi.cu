@@ -63,9 +63,9 @@ namespace gsv {
 static std::atomic<unsigned long long> g_launches{0};
 void count_launches(int k) { g_launches.fetch_add((unsigned long long)k); }
 
-static thread_local cudaEvent_t g_prof[3][2] = {};
+static std::atomic<cudaEvent_t> g_prof[3][2] = {};
 void profile_mark(int kind, bool stop, cudaStream_t stream) {
-    cudaEvent_t e = g_prof[kind][stop ? 1 : 0];
+    cudaEvent_t e = g_prof[kind][stop ? 1 : 0].load();
     if (e) cudaEventRecord(e, stream);
 }
 }  // namespace gsv

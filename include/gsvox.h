@@ -58,8 +58,9 @@ GSV_API const char *gsv_version(void);
  * counterpart. */
 GSV_API uint64_t gsv_launch_count(void);
 
-/* Install CUDA events (cudaEvent_t, passed as void*) that later calls on this
- * host thread record immediately before and after the main voxelization
+/* Install CUDA events (cudaEvent_t, passed as void*) that later calls from any
+ * host thread of the process record immediately before and after the main
+ * voxelization
  * kernel of kind `which` (0 = forward, 1 = per-Gaussian backward,
  * 2 = per-voxel backward), on the call's stream; NULL, NULL removes them.
  * Instrumentation for benchmarks; no reference counterpart. */

@@ -63,6 +63,17 @@ SIGNATURES = {
     "gsv_voxelize_backward_per_gaussian_slab": (
         ctypes.c_int, [_I3, _I32, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P,
                        _P, _P, _P, _P, _P, _SZ, _P]),
+    "gsv_l1_loss_workspace_bytes": (_SZ, [_I64]),
+    "gsv_l1_loss_forward": (
+        ctypes.c_int, [_I64, _P, _P, ctypes.c_float, _P, _P, _SZ, _P]),
+    "gsv_l1_loss_backward": (
+        ctypes.c_int, [_I64, _P, _P, _P, ctypes.c_float, _P, _P]),
+    "gsv_voxelize_forward_l1": (
+        ctypes.c_int, [_I3, _I32, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P,
+                       _P, ctypes.c_float, _P, _P, _P, _SZ, _P]),
+    "gsv_voxelize_backward_per_gaussian_l1": (
+        ctypes.c_int, [_I3, _I32, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P,
+                       _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _SZ, _P]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

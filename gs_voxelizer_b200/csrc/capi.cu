@@ -37,7 +37,9 @@ size_t vox_workspace_bytes(long long n, int channels, long long ntiles,
 cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
-                               float *out, void *ws, cudaStream_t stream);
+                               float *out, void *ws, cudaStream_t stream,
+                               const float *target, float *loss_out,
+                               double inv_denom);
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       long long nisect, const int *ids,
                                       const int *tile_bins,
@@ -46,7 +48,20 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       const float *intens, const float *grad,
                                       float *pos_grad, float *conic_grad,
                                       float *int_grad, void *ws,
-                                      cudaStream_t stream);
+                                      cudaStream_t stream,
+                                      const float *target,
+                                      const float *grad_loss,
+                                      float inv_denom);
+size_t l1_workspace_bytes(long long n);
+cudaError_t launch_sum(long long n, const float *a, const float *b,
+                       double inv_denom, float *out, void *ws,
+                       cudaStream_t stream);
+cudaError_t launch_l1_grad(long long n, const float *vol, const float *target,
+                           const float *grad_loss, float inv_denom,
+                           float *grad, cudaStream_t stream);
+cudaError_t launch_empty_l1(long long nvox, const float *target,
+                            double inv_denom, float *loss_out, void *ws,
+                            cudaStream_t stream);
 cudaError_t launch_vox_backward_voxel(const Geom &g, int C, int n,
                                       long long nisect, const int *ids,
                                       const int *tile_bins,
@@ -196,7 +211,8 @@ int forward_impl(const char *fn, const gsv::Geom &g, int32_t C, int32_t n,
     }
     return cuda_status(gsv::launch_vox_forward(g, C, n, ids, bins, pos, con,
                                                inten, out, ws,
-                                               as_stream(stream)),
+                                               as_stream(stream), nullptr,
+                                               nullptr, 1.0),
                        fn);
 }
 
@@ -219,7 +235,8 @@ int backward_impl(const char *fn, bool per_gaussian, const gsv::Geom &g,
             ? gsv::launch_vox_backward_gauss(g, C, n, nisect, ids, bins, pos,
                                              con, inten, grad, pos_grad,
                                              con_grad, int_grad, ws,
-                                             as_stream(stream))
+                                             as_stream(stream), nullptr,
+                                             nullptr, 1.f)
             : gsv::launch_vox_backward_voxel(g, C, n, nisect, ids, bins, pos,
                                              con, inten, grad, pos_grad,
                                              con_grad, int_grad, ws,
@@ -441,6 +458,102 @@ int gsv_voxelize_backward(const int32_t vol[3], int32_t C, int32_t n,
     return backward_impl(fn, false, gsv::make_geom(vol), C, n, nisect, ids,
                          bins, pos, con, inten, grad, pos_grad, con_grad,
                          int_grad, ws, ws_bytes, stream);
+}
+
+size_t gsv_l1_loss_workspace_bytes(int64_t n) {
+    return gsv::l1_workspace_bytes(n < 0 ? 0 : n);
+}
+
+int gsv_l1_loss_forward(int64_t n, const float *vol, const float *target,
+                        float denom, float *loss_out, void *ws,
+                        size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_l1_loss_forward";
+    GSV_REQUIRE(n >= 0 && loss_out && (n == 0 || (vol && target)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad arguments", fn);
+    GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
+    const size_t need = gsv::l1_workspace_bytes(n);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
+                need);
+    return cuda_status(gsv::launch_sum(n, vol, target, 1.0 / (double)denom,
+                                       loss_out, ws, as_stream(stream)),
+                       fn);
+}
+
+int gsv_l1_loss_backward(int64_t n, const float *vol, const float *target,
+                         const float *grad_loss, float denom, float *grad_vol,
+                         void *stream) {
+    const char *fn = "gsv_l1_loss_backward";
+    GSV_REQUIRE(n >= 0 && (n == 0 || (vol && target && grad_loss && grad_vol)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad arguments", fn);
+    GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
+    if (n == 0) return GSV_OK;
+    return cuda_status(gsv::launch_l1_grad(n, vol, target, grad_loss,
+                                           1.f / denom, grad_vol,
+                                           as_stream(stream)),
+                       fn);
+}
+
+int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
+                            int32_t C, int32_t n, int64_t nisect,
+                            const int32_t *ids, const int32_t *bins,
+                            const float *pos, const float *con,
+                            const float *inten, const float *target,
+                            float denom, float *out, float *loss_out,
+                            void *ws, size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_voxelize_forward_l1";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
+                               ws_bytes, ws);
+    if (st) return st;
+    const long long nvox =
+        (long long)(g.z_end() - g.z_begin()) * g.Y * g.X * C;
+    GSV_REQUIRE((out && target) || nvox == 0, GSV_ERR_INVALID_ARGUMENT,
+                "%s: out_vol or target is null", fn);
+    GSV_REQUIRE(loss_out && denom != 0.f, GSV_ERR_INVALID_ARGUMENT,
+                "%s: loss_out is null or denom is 0", fn);
+    cudaStream_t s = as_stream(stream);
+    if (nisect == 0) {
+        // empty volume: loss = sum |target| / denom
+        cudaError_t err = cudaMemsetAsync(out, 0, sizeof(float) * nvox, s);
+        if (err) return cuda_status(err, fn);
+        return cuda_status(gsv::launch_empty_l1(nvox, target,
+                                                1.0 / (double)denom, loss_out,
+                                                ws, s),
+                           fn);
+    }
+    return cuda_status(gsv::launch_vox_forward(g, C, n, ids, bins, pos, con,
+                                               inten, out, ws, s, target,
+                                               loss_out, 1.0 / (double)denom),
+                       fn);
+}
+
+int gsv_voxelize_backward_per_gaussian_l1(
+    const int32_t vol[3], int32_t tz0, int32_t tz1, int32_t C, int32_t n,
+    int64_t nisect, const int32_t *ids, const int32_t *bins, const float *pos,
+    const float *con, const float *inten, const float *out_vol,
+    const float *target, const float *grad_loss, float denom, float *pos_grad,
+    float *con_grad, float *int_grad, void *ws, size_t ws_bytes,
+    void *stream) {
+    const char *fn = "gsv_voxelize_backward_per_gaussian_l1";
+    if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
+    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
+                               ws_bytes, ws);
+    if (st) return st;
+    GSV_REQUIRE(n == 0 || (pos_grad && con_grad && int_grad),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null gradient output", fn);
+    GSV_REQUIRE(nisect == 0 || (out_vol && target && grad_loss),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null volume input", fn);
+    GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
+    return cuda_status(gsv::launch_vox_backward_gauss(
+                           g, C, n, nisect, ids, bins, pos, con, inten,
+                           out_vol, pos_grad, con_grad, int_grad, ws,
+                           as_stream(stream), target, grad_loss, 1.f / denom),
+                       fn);
 }
 
 }  // extern "C"

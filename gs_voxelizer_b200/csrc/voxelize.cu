@@ -8,13 +8,19 @@
 //                      the same sum w.r.t. mu, the six conic entries and I.
 //
 // The arithmetic is reorganised for the SM's issue rate (one warp
-// instruction per SMSP per clock, MUFU.EX2 at 16/clk/SM):
+// instruction per SMSP per clock; MUFU.EX2 at 16/clk/SM):
 //   * A per-Gaussian record is built once per call: centre, the conic scaled
 //     by log2(e) so that one ex2 gives exp(sigma), and the alpha*mean(I)
 //     cull rewritten as a threshold on the log2 exponent (s >= thr).
-//   * sigma restricted to a line of 8 voxels along z is a quadratic
-//     P + L*dz + C*dz^2; P and L are formed once per (Gaussian, column), so an
-//     evaluation costs 2-3 FP32 instructions, two compares and one ex2.
+//   * sigma along a line of 8 voxels in z is a quadratic P + L*dz + C*dz^2;
+//     P and L are formed once per (Gaussian, column), so an evaluation costs
+//     two FMAs, a compare and one ex2.
+//   * "sigma > 0" can only happen for a conic that is not positive definite
+//     or is so ill-conditioned that rounding flips the sign. The record marks
+//     Gaussians whose conic satisfies det(Q) >= 1e-5 trace(Q)^3 (so
+//     lambda_min / lambda_max >= 1e-5, far above the rounding error of the
+//     6-term quadratic); for them the test provably never fires and is
+//     skipped. Other Gaussians take the fully checked path.
 //   * Backward sums are factored: along a z column only sum(w), sum(w dz) and
 //     sum(w dz^2) are accumulated (w = alpha * dL/dvol); the six conic and
 //     three position sums are rebuilt from them with the column's dx, dy.
@@ -25,6 +31,10 @@ namespace gsv {
 cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *partials, int *tile_bins,
                                 cudaStream_t stream);
+size_t l1_workspace_bytes(long long n);
+cudaError_t launch_sum(long long n, const float *a, const float *b,
+                       double inv_denom, float *out, void *ws,
+                       cudaStream_t stream);
 
 namespace {
 
@@ -35,9 +45,15 @@ struct Rec {
     static constexpr int kF4 = C <= 2 ? 3 : 4;  // float4 per record
 };
 
+__device__ __forceinline__ bool robust_flag(float thr) {
+    return (__float_as_uint(thr) & 1u) != 0u;
+}
+
 // record: r0 = (mx, my, mz, thr), r1 = (A, B, Cz, D), r2 = (E, F, I0, I1),
 //         r3 = (I2, I3, 0, 0)  with
-// s = A dx^2 + B dy^2 + Cz dz^2 + D dx dy + E dx dz + F dy dz = log2(e) sigma
+// s = A dx^2 + B dy^2 + Cz dz^2 + D dx dy + E dx dz + F dy dz = log2(e) sigma.
+// The lowest mantissa bit of thr carries the "robustly positive definite"
+// flag (1 ulp of the threshold; the cull is already approximate there).
 template <int C>
 __global__ void __launch_bounds__(256)
 prep_records_kernel(int n, const float4 *__restrict__ pos_radii,
@@ -66,6 +82,20 @@ prep_records_kernel(int n, const float4 *__restrict__ pos_radii,
     } else {
         thr = __int_as_float(0xff800000);  // NaN mean: -inf, output is NaN
     }
+    // robust positive definiteness of Q = [[a b c][b d e][c e f]]
+    const double a = ab.x, b = ab.y, c = cd.x, d = cd.y, e = ef.x, f = ef.y;
+    const double m2 = a * d - b * b;
+    const double det = a * (d * f - e * e) - b * (b * f - e * c) +
+                       c * (b * e - d * c);
+    const double tr = a + d + f;
+    const bool robust = a > 0.0 && m2 > 0.0 && det > 0.0 &&
+                        det >= 1e-5 * tr * tr * tr && isfinite(det) &&
+                        isfinite(tr);
+    if (isfinite(thr)) {
+        unsigned bits = __float_as_uint(thr);
+        bits = robust ? (bits | 1u) : (bits & ~1u);
+        thr = __uint_as_float(bits);
+    }
     const float h = -0.5f * kLog2e;
     rec[i * R + 0] = make_float4(p.x, p.y, p.z, thr);
     rec[i * R + 1] =
@@ -85,19 +115,98 @@ __device__ __forceinline__ void tile_coords(const Geom &g, long long tile,
     oz = tz * kTile;
 }
 
-// ---------------------------------------------------------------- forward
+template <int C>
+__device__ __forceinline__ void record_intensity(const float4 &r2,
+                                                 const float4 &r3,
+                                                 float (&I)[C]) {
+    I[0] = r2.z;
+    if (C > 1) I[1 % C] = r2.w;
+    if (C > 2) I[2 % C] = r3.x;
+    if (C > 3) I[3 % C] = r3.y;
+}
 
-constexpr int kFwdThreads = 64;  // one thread per (x, y) column of a tile
-constexpr int kFwdBatch = 128;   // Gaussian records staged per pass
+// ---------------------------------------------------------------- forward
+//
+// One warp per tile. Lane (x, y) with x = lane & 7, y = lane >> 3 owns the
+// two z-columns (x, y) and (x, y + 4): 16 voxels. Gaussian records are
+// staged in shared memory in batches, tile-relative, together with the eight
+// z-offsets dz_j = mz - (j + 0.5) every lane needs.
+
+constexpr int kFwdBatch = 64;
+
+// acc += I * a when thr <= s (and s <= 0 when CHECK_SIGN): one compare and
+// one predicated FMA.
+template <bool CHECK_SIGN>
+__device__ __forceinline__ void fma_if_valid(float &acc, float I, float a,
+                                             float s, float thr) {
+    if (CHECK_SIGN) {
+        asm("{\n\t.reg .pred p;\n\t"
+            "setp.ge.f32 p, %1, %2;\n\t"
+            "setp.le.and.f32 p, %1, 0f00000000, p;\n\t"
+            "@p fma.rn.f32 %0, %3, %4, %0;\n\t}"
+            : "+f"(acc) : "f"(s), "f"(thr), "f"(I), "f"(a));
+    } else {
+        asm("{\n\t.reg .pred p;\n\t"
+            "setp.ge.f32 p, %1, %2;\n\t"
+            "@p fma.rn.f32 %0, %3, %4, %0;\n\t}"
+            : "+f"(acc) : "f"(s), "f"(thr), "f"(I), "f"(a));
+    }
+}
 
 template <int C>
-__global__ void __launch_bounds__(kFwdThreads, C <= 2 ? 16 : 8)
+__device__ __forceinline__ void fwd_column_pair(
+    const float4 &r0, const float4 &r1, const float4 &r2,
+    const float (&dz)[8], const float (&I)[C], float fx, float fy,
+    bool check_sign, float (&acc)[2][8][C]) {
+    const float thr = r0.w;
+    const float dx = r0.x - fx;
+    const float dy0 = r0.y - fy;
+    const float dy1 = dy0 - 4.f;
+    const float Adx = r1.x * dx, Edx = r2.x * dx;
+    const float P0 = fmaf(dx, fmaf(r1.w, dy0, Adx), r1.y * dy0 * dy0);
+    const float L0 = fmaf(r2.y, dy0, Edx);
+    const float P1 = fmaf(dx, fmaf(r1.w, dy1, Adx), r1.y * dy1 * dy1);
+    const float L1 = fmaf(r2.y, dy1, Edx);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float s0 = fmaf(dz[j], fmaf(r1.z, dz[j], L0), P0);
+        const float s1 = fmaf(dz[j], fmaf(r1.z, dz[j], L1), P1);
+        const float a0 = ex2(s0), a1 = ex2(s1);
+        if (C == 1) {
+            if (check_sign) {
+                fma_if_valid<true>(acc[0][j][0], I[0], a0, s0, thr);
+                fma_if_valid<true>(acc[1][j][0], I[0], a1, s1, thr);
+            } else {
+                fma_if_valid<false>(acc[0][j][0], I[0], a0, s0, thr);
+                fma_if_valid<false>(acc[1][j][0], I[0], a1, s1, thr);
+            }
+        } else {
+            bool ok0 = s0 >= thr, ok1 = s1 >= thr;
+            if (check_sign) {
+                ok0 &= s0 <= 0.f;
+                ok1 &= s1 <= 0.f;
+            }
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                if (ok0) acc[0][j][c] = fmaf(I[c], a0, acc[0][j][c]);
+                if (ok1) acc[1][j][c] = fmaf(I[c], a1, acc[1][j][c]);
+            }
+        }
+    }
+}
+
+// LOSS: also reduce sum |vol - target| over the tile's voxels into
+// tile_loss[tile] (the fused L1 loss; target has the output's layout).
+template <int C, bool LOSS>
+__global__ void __launch_bounds__(32, C <= 2 ? 32 : 16)
 vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                const int *__restrict__ ids, const float4 *__restrict__ rec,
-               float *__restrict__ out) {
+               float *__restrict__ out, const float *__restrict__ target,
+               float *__restrict__ tile_loss) {
     constexpr int R = Rec<C>::kF4;
-    constexpr int kStage = (kFwdBatch * R * 4 > kTileVoxels * C)
-                               ? kFwdBatch * R * 4
+    constexpr int RS = R + 2;  // record + 8 dz
+    constexpr int kStage = (kFwdBatch * RS * 4 > kTileVoxels * C)
+                               ? kFwdBatch * RS * 4
                                : kTileVoxels * C;
     __shared__ __align__(16) float smem[kStage];
     float4 *sb = reinterpret_cast<float4 *>(smem);
@@ -105,70 +214,70 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
     const long long tile = blockIdx.x;
     int ox, oy, oz;
     tile_coords(g, tile, ox, oy, oz);
-    const int lx = threadIdx.x & 7, ly = threadIdx.x >> 3;
+    const int lane = threadIdx.x;
+    const int lx = lane & 7, ly = lane >> 3;
     const float fx = lx + 0.5f, fy = ly + 0.5f;
 
-    float acc[8][C];
+    float acc[2][8][C];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int c = 0; c < C; ++c) acc[j][c] = 0.f;
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int c = 0; c < C; ++c) acc[k][j][c] = 0.f;
 
     const int2 range = bins[tile];
     for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
         const int nb = min(kFwdBatch, range.y - s0);
-        __syncthreads();
-        for (int k = threadIdx.x; k < nb; k += kFwdThreads) {
+        __syncwarp();
+        for (int k = lane; k < nb; k += 32) {
             const int gid = ids[s0 + k];
             float4 r0 = rec[(size_t)gid * R];
             r0.x -= (float)ox;
             r0.y -= (float)oy;
             r0.z -= (float)oz;
-            sb[k * R] = r0;
+            sb[k * RS] = r0;
 #pragma unroll
-            for (int q = 1; q < R; ++q) sb[k * R + q] = rec[(size_t)gid * R + q];
+            for (int q = 1; q < R; ++q) sb[k * RS + q] = rec[(size_t)gid * R + q];
+            sb[k * RS + R] = make_float4(r0.z - 0.5f, r0.z - 1.5f, r0.z - 2.5f,
+                                         r0.z - 3.5f);
+            sb[k * RS + R + 1] = make_float4(r0.z - 4.5f, r0.z - 5.5f,
+                                             r0.z - 6.5f, r0.z - 7.5f);
         }
-        __syncthreads();
+        __syncwarp();
 #pragma unroll 1
         for (int t = 0; t < nb; ++t) {
-            const float4 r0 = sb[t * R + 0];
-            const float4 r1 = sb[t * R + 1];
-            const float4 r2 = sb[t * R + 2];
+            const float4 r0 = sb[t * RS + 0];
+            const float4 r1 = sb[t * RS + 1];
+            const float4 r2 = sb[t * RS + 2];
+            const float4 r3 = (R == 4) ? sb[t * RS + 3] : r2;
+            const float4 za = sb[t * RS + R], zb = sb[t * RS + R + 1];
+            const float dz[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
             float I[C];
-            I[0] = r2.z;
-            if (C > 1) I[1 % C] = r2.w;
-            if (C > 2) {
-                const float4 r3 = sb[t * R + 3];
-                I[2 % C] = r3.x;
-                if (C > 3) I[3 % C] = r3.y;
-            }
-            const float dx = r0.x - fx, dy = r0.y - fy;
-            const float P = fmaf(dx, fmaf(r1.x, dx, r1.w * dy), r1.y * dy * dy);
-            const float L = fmaf(r2.x, dx, r2.y * dy);
-            const float thr = r0.w;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float dz = r0.z - ((float)j + 0.5f);
-                const float s = fmaf(dz, fmaf(r1.z, dz, L), P);
-                const bool ok = (s <= 0.f) & (s >= thr);
-                const float a = ex2(s);
-#pragma unroll
-                for (int c = 0; c < C; ++c)
-                    acc[j][c] = ok ? fmaf(I[c], a, acc[j][c]) : acc[j][c];
-            }
+            record_intensity<C>(r2, r3, I);
+            if (robust_flag(r0.w))
+                fwd_column_pair<C>(r0, r1, r2, dz, I, fx, fy, false, acc);
+            else
+                fwd_column_pair<C>(r0, r1, r2, dz, I, fx, fy, true, acc);
         }
     }
 
     // stage the 8x8x8xC block and store it row by row (x fastest)
-    __syncthreads();
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int c = 0; c < C; ++c)
-            smem[((j * 64) + ly * 8 + lx) * C + c] = acc[j][c];
-    __syncthreads();
-    {
-        const int row = threadIdx.x;  // 64 rows = 8 z * 8 y
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+                smem[((j * 64) + (ly + 4 * k) * 8 + lx) * C + c] = acc[k][j][c];
+    __syncwarp();
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
+                        (!LOSS || (reinterpret_cast<uintptr_t>(target) & 15) == 0);
+    float lsum = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = lane + 32 * h;  // 64 rows = 8 z * 8 y
         const int z = oz + (row >> 3), y = oy + (row & 7);
         if (z < g.z_end() && y < g.Y) {
             const int nx = min(kTile, g.X - ox);
@@ -176,16 +285,31 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                 (((size_t)(z - g.z_begin()) * g.Y + y) * g.X + ox) * C;
             const float *src = smem + row * 8 * C;
             float *dst = out + base;
-            if (nx == kTile && ((base & 3) == 0) &&
-                ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+            if (nx == kTile && ((base & 3) == 0) && vec_ok) {
 #pragma unroll
-                for (int q = 0; q < 2 * C; ++q)
-                    reinterpret_cast<float4 *>(dst)[q] =
-                        reinterpret_cast<const float4 *>(src)[q];
+                for (int q = 0; q < 2 * C; ++q) {
+                    const float4 v = reinterpret_cast<const float4 *>(src)[q];
+                    reinterpret_cast<float4 *>(dst)[q] = v;
+                    if (LOSS) {
+                        const float4 t = __ldg(
+                            reinterpret_cast<const float4 *>(target + base) + q);
+                        lsum += fabsf(v.x - t.x) + fabsf(v.y - t.y) +
+                                fabsf(v.z - t.z) + fabsf(v.w - t.w);
+                    }
+                }
             } else {
-                for (int q = 0; q < nx * C; ++q) dst[q] = src[q];
+                for (int q = 0; q < nx * C; ++q) {
+                    dst[q] = src[q];
+                    if (LOSS) lsum += fabsf(src[q] - __ldg(target + base + q));
+                }
             }
         }
+    }
+    if (LOSS) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        if (lane == 0) tile_loss[tile] = lsum;
     }
 }
 
@@ -209,11 +333,15 @@ struct BwdSmem {
     static constexpr int kWarp = 8 * kRow;          // floats per warp buffer
 };
 
-template <int C>
+// Stages dL/dvol of one tile. LOSS: dL/dvol is not materialised; it is the
+// fused L1 gradient sign(vol - target) * scale, computed from the volume
+// (passed as `grad`) and the target here.
+template <int C, bool LOSS>
 __device__ __forceinline__ void stage_grad_tile(const Geom &g,
                                                 const float *__restrict__ grad,
-                                                int ox, int oy, int oz,
-                                                float *buf, int lane) {
+                                                const float *__restrict__ target,
+                                                float scale, int ox, int oy,
+                                                int oz, float *buf, int lane) {
     using S = BwdSmem<C>;
     // 64 (z, y) rows of 8*C floats; lane handles rows lane and lane + 32
 #pragma unroll
@@ -227,7 +355,8 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
         const size_t base =
             row_in ? (((size_t)(z - g.z_begin()) * g.Y + y) * g.X + ox) * C : 0;
         if (nx == kTile && (base & 3) == 0 &&
-            ((reinterpret_cast<uintptr_t>(grad) & 15) == 0)) {
+            ((reinterpret_cast<uintptr_t>(grad) & 15) == 0) &&
+            (!LOSS || (reinterpret_cast<uintptr_t>(target) & 15) == 0)) {
 #pragma unroll
             for (int q = 0; q < 2 * C; ++q) {
                 const float4 t =
@@ -236,11 +365,26 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
                 v[4 * q + 1] = t.y;
                 v[4 * q + 2] = t.z;
                 v[4 * q + 3] = t.w;
+                if (LOSS) {
+                    const float4 u =
+                        __ldg(reinterpret_cast<const float4 *>(target + base) + q);
+                    v[4 * q + 0] -= u.x;
+                    v[4 * q + 1] -= u.y;
+                    v[4 * q + 2] -= u.z;
+                    v[4 * q + 3] -= u.w;
+                }
             }
         } else {
 #pragma unroll
-            for (int q = 0; q < 8 * C; ++q)
+            for (int q = 0; q < 8 * C; ++q) {
                 v[q] = (q < nx * C) ? __ldg(grad + base + q) : 0.f;
+                if (LOSS) v[q] -= (q < nx * C) ? __ldg(target + base + q) : 0.f;
+            }
+        }
+        if (LOSS) {
+#pragma unroll
+            for (int q = 0; q < 8 * C; ++q)
+                v[q] = v[q] > 0.f ? scale : (v[q] < 0.f ? -scale : 0.f);
         }
 #pragma unroll
         for (int x = 0; x < 8; ++x)
@@ -250,8 +394,94 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
     }
 }
 
-template <int C>
-__global__ void __launch_bounds__(kBwdWarps * 32)
+// Sums over one y-row of the tile for one Gaussian (per lane).
+struct RowSums {
+    float R0, R1, R2, Rx0, Rxx, Rx1;
+};
+
+template <int C, bool CHECK_SIGN>
+__device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
+                                           float thr, float A, float Cz,
+                                           float E, float Dy, float By2,
+                                           float Fy, const float (&dz)[8],
+                                           const float (&dz2)[8],
+                                           const float (&I)[C],
+                                           float (&W)[C]) {
+    using S = BwdSmem<C>;
+    RowSums r = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+        const float dx = mx - ((float)x + 0.5f);
+        const float P = fmaf(dx, fmaf(A, dx, Dy), By2);
+        const float L = fmaf(E, dx, Fy);
+        float gv[8 * C];
+#pragma unroll
+        for (int q4 = 0; q4 < 2 * C; ++q4) {
+            const float4 t =
+                reinterpret_cast<const float4 *>(colbase + x * S::kCol)[q4];
+            gv[4 * q4 + 0] = t.x;
+            gv[4 * q4 + 1] = t.y;
+            gv[4 * q4 + 2] = t.z;
+            gv[4 * q4 + 3] = t.w;
+        }
+        float T0 = 0.f, T1 = 0.f, T2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float s = fmaf(dz[j], fmaf(Cz, dz[j], L), P);
+            if (C == 1) {
+                // w = alpha * dL/dvol; the three moment updates are
+                // predicated on the cull test (no select instruction)
+                const float w = ex2(s) * gv[j];
+                if (CHECK_SIGN) {
+                    asm("{\n\t.reg .pred p;\n\t"
+                        "setp.ge.f32 p, %3, %4;\n\t"
+                        "setp.le.and.f32 p, %3, 0f00000000, p;\n\t"
+                        "@p add.f32 %0, %0, %5;\n\t"
+                        "@p fma.rn.f32 %1, %5, %6, %1;\n\t"
+                        "@p fma.rn.f32 %2, %5, %7, %2;\n\t}"
+                        : "+f"(T0), "+f"(T1), "+f"(T2)
+                        : "f"(s), "f"(thr), "f"(w), "f"(dz[j]), "f"(dz2[j]));
+                } else {
+                    asm("{\n\t.reg .pred p;\n\t"
+                        "setp.ge.f32 p, %3, %4;\n\t"
+                        "@p add.f32 %0, %0, %5;\n\t"
+                        "@p fma.rn.f32 %1, %5, %6, %1;\n\t"
+                        "@p fma.rn.f32 %2, %5, %7, %2;\n\t}"
+                        : "+f"(T0), "+f"(T1), "+f"(T2)
+                        : "f"(s), "f"(thr), "f"(w), "f"(dz[j]), "f"(dz2[j]));
+                }
+                continue;
+            }
+            bool ok = s >= thr;
+            if (CHECK_SIGN) ok &= s <= 0.f;
+            const float a = ok ? ex2(s) : 0.f;
+            float w;
+            {
+                float h = I[0] * gv[j * C];
+#pragma unroll
+                for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[j * C + c], h);
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    W[c] = fmaf(a, gv[j * C + c], W[c]);
+                w = a * h;
+            }
+            T0 += w;
+            T1 = fmaf(w, dz[j], T1);
+            T2 = fmaf(w, dz2[j], T2);
+        }
+        r.R0 += T0;
+        r.R1 += T1;
+        r.R2 += T2;
+        const float u = dx * T0;
+        r.Rx0 += u;
+        r.Rxx = fmaf(u, dx, r.Rxx);
+        r.Rx1 = fmaf(dx, T1, r.Rx1);
+    }
+    return r;
+}
+
+template <int C, bool LOSS>
+__global__ void __launch_bounds__(kBwdWarps * 32, C <= 2 ? 6 : 4)
 vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
                      const int *__restrict__ ids,
                      const float4 *__restrict__ rec,
@@ -263,13 +493,16 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
                      int *__restrict__ work_counter,
                      float *__restrict__ pos_grad,
                      float *__restrict__ conic_grad,
-                     float *__restrict__ int_grad) {
+                     float *__restrict__ int_grad,
+                     const float *__restrict__ target,
+                     const float *__restrict__ grad_loss, float inv_denom) {
     using S = BwdSmem<C>;
     constexpr int R = Rec<C>::kF4;
     __shared__ __align__(16) float smem[kBwdWarps * S::kWarp];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     float *buf = smem + wid * S::kWarp;
     const int total = (int)*item_total;
+    const float scale = LOSS ? (*grad_loss) * inv_denom : 0.f;
 
     while (true) {
         int item = 0;
@@ -293,11 +526,12 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
         int ox, oy, oz;
         tile_coords(g, tile, ox, oy, oz);
         __syncwarp();
-        stage_grad_tile<C>(g, grad, ox, oy, oz, buf, lane);
+        stage_grad_tile<C, LOSS>(g, grad, target, scale, ox, oy, oz, buf, lane);
         __syncwarp();
 
         int gid = 0;
-        float4 r0 = make_float4(0.f, 0.f, 0.f, __int_as_float(0x7f800000));
+        // invalid lanes get thr = +inf with the robust bit: nothing passes
+        float4 r0 = make_float4(0.f, 0.f, 0.f, __int_as_float(0x7f800001));
         float4 r1 = make_float4(0.f, 0.f, 0.f, 0.f), r2 = r1, r3 = r1;
         if (valid) {
             gid = ids[start + gi];
@@ -310,16 +544,14 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
             r0.z -= (float)oz;
         }
         float I[C];
-        I[0] = r2.z;
-        if (C > 1) I[1 % C] = r2.w;
-        if (C > 2) I[2 % C] = r3.x;
-        if (C > 3) I[3 % C] = r3.y;
+        record_intensity<C>(r2, r3, I);
         const float thr = r0.w;
-        float dz[8], cdz[8];
+        const bool all_robust = __all_sync(0xffffffffu, robust_flag(thr));
+        float dz[8], dz2[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             dz[j] = r0.z - ((float)j + 0.5f);
-            cdz[j] = r1.z * dz[j];
+            dz2[j] = dz[j] * dz[j];
         }
 
         // sums over the Gaussian's voxels of w-weighted monomials of d, where
@@ -335,65 +567,23 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
             const int yl = sub * rows + q;
             const float dy = r0.y - ((float)yl + 0.5f);
             const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
-            float R0 = 0.f, R1 = 0.f, R2 = 0.f, Rx0 = 0.f, Rxx = 0.f, Rx1 = 0.f;
             const float *colbase = buf + yl * S::kRow;
-#pragma unroll
-            for (int x = 0; x < 8; ++x) {
-                const float dx = r0.x - ((float)x + 0.5f);
-                const float P = fmaf(dx, fmaf(r1.x, dx, Dy), By2);
-                const float L = fmaf(r2.x, dx, Fy);
-                float gv[8 * C];
-#pragma unroll
-                for (int q4 = 0; q4 < 2 * C; ++q4) {
-                    const float4 t = reinterpret_cast<const float4 *>(
-                        colbase + x * S::kCol)[q4];
-                    gv[4 * q4 + 0] = t.x;
-                    gv[4 * q4 + 1] = t.y;
-                    gv[4 * q4 + 2] = t.z;
-                    gv[4 * q4 + 3] = t.w;
-                }
-                float T0 = 0.f, T1 = 0.f, T2 = 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float s = fmaf(dz[j], cdz[j] + L, P);
-                    const bool ok = (s <= 0.f) & (s >= thr);
-                    const float a = ok ? ex2(s) : 0.f;
-                    float w;
-                    if (C == 1) {
-                        w = a * gv[j];  // intensity grad = sum(w) = sum(R0)
-                    } else {
-                        float h = I[0] * gv[j * C];
-#pragma unroll
-                        for (int c = 1; c < C; ++c)
-                            h = fmaf(I[c], gv[j * C + c], h);
-#pragma unroll
-                        for (int c = 0; c < C; ++c)
-                            W[c] = fmaf(a, gv[j * C + c], W[c]);
-                        w = a * h;
-                    }
-                    T0 += w;
-                    const float t = w * dz[j];
-                    T1 += t;
-                    T2 = fmaf(t, dz[j], T2);
-                }
-                R0 += T0;
-                R1 += T1;
-                R2 += T2;
-                const float u = dx * T0;
-                Rx0 += u;
-                Rxx = fmaf(u, dx, Rxx);
-                Rx1 = fmaf(dx, T1, Rx1);
-            }
-            if (C == 1) W[0] += R0;
-            Sxx += Rxx;
-            Szz += R2;
-            Sxz += Rx1;
-            Vx += Rx0;
-            Vz += R1;
-            Syy = fmaf(dy * dy, R0, Syy);
-            Sxy = fmaf(dy, Rx0, Sxy);
-            Syz = fmaf(dy, R1, Syz);
-            Vy = fmaf(dy, R0, Vy);
+            const RowSums rs =
+                all_robust
+                    ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
+                                        Dy, By2, Fy, dz, dz2, I, W)
+                    : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
+                                       Dy, By2, Fy, dz, dz2, I, W);
+            if (C == 1) W[0] += rs.R0;  // intensity grad = sum(w) (C = 1)
+            Sxx += rs.Rxx;
+            Szz += rs.R2;
+            Sxz += rs.Rx1;
+            Vx += rs.Rx0;
+            Vz += rs.R1;
+            Syy = fmaf(dy * dy, rs.R0, Syy);
+            Sxy = fmaf(dy, rs.Rx0, Sxy);
+            Syz = fmaf(dy, rs.R1, Syz);
+            Vy = fmaf(dy, rs.R0, Vy);
         }
 
         // combine row groups (lanes gi, gi+gs, gi+2gs, ...)
@@ -464,12 +654,15 @@ item_fill_kernel(const int2 *__restrict__ item_bins, long long ntiles,
 // ------------------------------------------------------ backward (per voxel)
 //
 // Voxel-centric variant (the reference's use_per_gaussian_backward=False):
-// the forward's CTA layout, one thread per (x, y) column of 8 voxels; each
-// thread folds its column into the per-Gaussian sums, the warp reduces them,
-// and lane 0 issues one set of vector atomics per warp and Gaussian.
+// one CTA of 64 threads per tile, one thread per (x, y) column of 8 voxels;
+// each thread folds its column into the per-Gaussian sums, the warp reduces
+// them, and lane 0 issues one set of vector atomics per warp and Gaussian.
+
+constexpr int kVoxThreads = 64;
+constexpr int kVoxBatch = 128;
 
 template <int C>
-__global__ void __launch_bounds__(kFwdThreads, C <= 2 ? 16 : 8)
+__global__ void __launch_bounds__(kVoxThreads, C <= 2 ? 16 : 8)
 vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
                      const int *__restrict__ ids,
                      const float4 *__restrict__ rec,
@@ -479,8 +672,8 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
                      float *__restrict__ conic_grad,
                      float *__restrict__ int_grad) {
     constexpr int R = Rec<C>::kF4;
-    __shared__ __align__(16) float4 sb[kFwdBatch * R];
-    __shared__ int sid[kFwdBatch];
+    __shared__ __align__(16) float4 sb[kVoxBatch * R];
+    __shared__ int sid[kVoxBatch];
 
     const long long tile = blockIdx.x;
     int ox, oy, oz;
@@ -505,10 +698,10 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
     }
 
     const int2 range = bins[tile];
-    for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
-        const int nb = min(kFwdBatch, range.y - s0);
+    for (int s0 = range.x; s0 < range.y; s0 += kVoxBatch) {
+        const int nb = min(kVoxBatch, range.y - s0);
         __syncthreads();
-        for (int k = threadIdx.x; k < nb; k += kFwdThreads) {
+        for (int k = threadIdx.x; k < nb; k += kVoxThreads) {
             const int gid = ids[s0 + k];
             sid[k] = gid;
             float4 r0 = rec[(size_t)gid * R];
@@ -525,18 +718,14 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
             const float4 r0 = sb[t * R + 0];
             const float4 r1 = sb[t * R + 1];
             const float4 r2 = sb[t * R + 2];
+            const float4 r3 = (R == 4) ? sb[t * R + 3] : r2;
             float I[C];
-            I[0] = r2.z;
-            if (C > 1) I[1 % C] = r2.w;
-            if (C > 2) {
-                const float4 r3 = sb[t * R + 3];
-                I[2 % C] = r3.x;
-                if (C > 3) I[3 % C] = r3.y;
-            }
+            record_intensity<C>(r2, r3, I);
             const float dx = r0.x - fx, dy = r0.y - fy;
             const float P = fmaf(dx, fmaf(r1.x, dx, r1.w * dy), r1.y * dy * dy);
             const float L = fmaf(r2.x, dx, r2.y * dy);
             const float thr = r0.w;
+            const bool check_sign = !robust_flag(thr);
             float T0 = 0.f, T1 = 0.f, T2 = 0.f;
             float W[C];
 #pragma unroll
@@ -546,7 +735,7 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
             for (int j = 0; j < 8; ++j) {
                 const float dz = r0.z - ((float)j + 0.5f);
                 const float s = fmaf(dz, fmaf(r1.z, dz, L), P);
-                const bool ok = (s <= 0.f) & (s >= thr);
+                const bool ok = (s >= thr) & (!check_sign | (s <= 0.f));
                 const float a = ok ? ex2(s) : 0.f;
                 float h = I[0] * gv[j][0];
 #pragma unroll
@@ -604,7 +793,8 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
 // ------------------------------------------------------------ host launchers
 
 struct VoxLayout {
-    size_t rec, item_counts, item_bins, partials, item_tile, counter, total;
+    size_t rec, item_counts, item_bins, partials, item_tile, counter,
+        tile_loss, loss_partials, total;
 };
 
 static inline size_t align256v(size_t x) { return (x + 255) & ~size_t(255); }
@@ -628,6 +818,10 @@ VoxLayout vox_layout(long long n, int channels, long long ntiles,
     off = align256v(off + sizeof(int) * (size_t)(max_items + 1));
     L.counter = off;
     off = align256v(off + sizeof(int) * 4);
+    L.tile_loss = off;
+    off = align256v(off + sizeof(float) * (size_t)(ntiles > 0 ? ntiles : 1));
+    L.loss_partials = off;  // sized for any reduction (<= kSMs*8 blocks)
+    off = align256v(off + l1_workspace_bytes(1LL << 40));
     L.total = off;
     return L;
 }
@@ -655,38 +849,73 @@ static cudaError_t launch_prep(int n, int C, const float *pos_radii,
     return cudaGetLastError();
 }
 
+template <int C, bool LOSS>
+static void fwd_launch(unsigned grid, cudaStream_t stream, const Geom &g,
+                       const int2 *bins, const int *ids, const float4 *rec,
+                       float *out, const float *target, float *tile_loss) {
+    vox_fwd_kernel<C, LOSS><<<grid, 32, 0, stream>>>(g, bins, ids, rec, out,
+                                                     target, tile_loss);
+}
+
+// target != nullptr: fused L1, loss_out[0] = sum |vol - target| * inv_denom
 cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
-                               float *out, void *ws, cudaStream_t stream) {
+                               float *out, void *ws, cudaStream_t stream,
+                               const float *target, float *loss_out,
+                               double inv_denom) {
     const long long ntiles = g.slab_tiles();
     const VoxLayout L = vox_layout(n, C, ntiles, 0);
-    float4 *rec = reinterpret_cast<float4 *>(static_cast<char *>(ws) + L.rec);
+    char *base = static_cast<char *>(ws);
+    float4 *rec = reinterpret_cast<float4 *>(base + L.rec);
+    float *tile_loss = reinterpret_cast<float *>(base + L.tile_loss);
     cudaError_t err = launch_prep(n, C, pos_radii, conics, intens, rec, stream);
     if (err) return err;
-    if (ntiles == 0) return cudaSuccess;
+    if (ntiles == 0) {
+        if (target) return cudaMemsetAsync(loss_out, 0, sizeof(float), stream);
+        return cudaSuccess;
+    }
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
     const unsigned grid = (unsigned)ntiles;
     profile_mark(kProfForward, false, stream);
-    switch (C) {
-        case 1: vox_fwd_kernel<1><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
-        case 2: vox_fwd_kernel<2><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
-        case 3: vox_fwd_kernel<3><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
-        case 4: vox_fwd_kernel<4><<<grid, kFwdThreads, 0, stream>>>(g, bins, ids, rec, out); break;
+    const bool loss = target != nullptr;
+    switch (C * 2 + (loss ? 1 : 0)) {
+        case 2: fwd_launch<1, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 3: fwd_launch<1, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 4: fwd_launch<2, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 5: fwd_launch<2, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 6: fwd_launch<3, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 7: fwd_launch<3, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 8: fwd_launch<4, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 9: fwd_launch<4, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
         default: return cudaErrorInvalidValue;
     }
     profile_mark(kProfForward, true, stream);
     count_launches(1);
-    return cudaGetLastError();
+    if ((err = cudaGetLastError())) return err;
+    if (loss)
+        return launch_sum(ntiles, tile_loss, nullptr, inv_denom, loss_out,
+                          base + L.loss_partials, stream);
+    return cudaSuccess;
 }
 
-template <int C>
+// Fused-L1 forward of an empty tile list: the volume is zero, so the loss is
+// sum |target| * inv_denom.
+cudaError_t launch_empty_l1(long long nvox, const float *target,
+                            double inv_denom, float *loss_out, void *ws,
+                            cudaStream_t stream) {
+    const VoxLayout L = vox_layout(0, 1, 0, 0);
+    return launch_sum(nvox, target, nullptr, inv_denom, loss_out,
+                      static_cast<char *>(ws) + L.loss_partials, stream);
+}
+
+template <int C, bool LOSS>
 static int bwd_gauss_grid() {
     static int cached = 0;
     if (cached) return cached;
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, vox_bwd_gauss_kernel<C>, kBwdWarps * 32, 0);
+        &per_sm, vox_bwd_gauss_kernel<C, LOSS>, kBwdWarps * 32, 0);
     int dev = 0, sms = kSMs;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -694,6 +923,21 @@ static int bwd_gauss_grid() {
     return cached;
 }
 
+template <int C, bool LOSS>
+static void bwd_launch(cudaStream_t stream, const Geom &g, const int2 *bins,
+                       const int *ids, const float4 *rec, const float2 *cq,
+                       const float *grad, const int2 *ib, const int *item_tile,
+                       const long long *total, int *counter, float *pos_grad,
+                       float *conic_grad, float *int_grad, const float *target,
+                       const float *grad_loss, float inv_denom) {
+    vox_bwd_gauss_kernel<C, LOSS><<<bwd_gauss_grid<C, LOSS>(), kBwdWarps * 32,
+                                    0, stream>>>(
+        g, bins, ids, rec, cq, grad, ib, item_tile, total, counter, pos_grad,
+        conic_grad, int_grad, target, grad_loss, inv_denom);
+}
+
+// target != nullptr: fused L1; `grad` is then the forward volume and
+// dL/dvol = sign(vol - target) * grad_loss[0] * inv_denom.
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       long long nisect, const int *ids,
                                       const int *tile_bins,
@@ -702,7 +946,10 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       const float *intens, const float *grad,
                                       float *pos_grad, float *conic_grad,
                                       float *int_grad, void *ws,
-                                      cudaStream_t stream) {
+                                      cudaStream_t stream,
+                                      const float *target,
+                                      const float *grad_loss,
+                                      float inv_denom) {
     const long long ntiles = g.slab_tiles();
     const VoxLayout L = vox_layout(n, C, ntiles, nisect);
     char *base = static_cast<char *>(ws);
@@ -731,21 +978,25 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     const long long *total = partials + nblocks;
     const float2 *cq = reinterpret_cast<const float2 *>(conics);
     const int2 *ib = reinterpret_cast<const int2 *>(item_bins);
-#define GSV_BWD(Cc)                                                          \
-    vox_bwd_gauss_kernel<Cc><<<bwd_gauss_grid<Cc>(), kBwdWarps * 32, 0,      \
-                               stream>>>(g, bins, ids, rec, cq, grad, ib,    \
-                                         item_tile, total, counter,          \
-                                         pos_grad, conic_grad, int_grad)
+    const bool loss = target != nullptr;
     profile_mark(kProfBackwardGauss, false, stream);
-    switch (C) {
-        case 1: GSV_BWD(1); break;
-        case 2: GSV_BWD(2); break;
-        case 3: GSV_BWD(3); break;
-        case 4: GSV_BWD(4); break;
+#define GSV_BWD(Cc, Ll)                                                       \
+    bwd_launch<Cc, Ll>(stream, g, bins, ids, rec, cq, grad, ib, item_tile,    \
+                       total, counter, pos_grad, conic_grad, int_grad, target, \
+                       grad_loss, inv_denom)
+    switch (C * 2 + (loss ? 1 : 0)) {
+        case 2: GSV_BWD(1, false); break;
+        case 3: GSV_BWD(1, true); break;
+        case 4: GSV_BWD(2, false); break;
+        case 5: GSV_BWD(2, true); break;
+        case 6: GSV_BWD(3, false); break;
+        case 7: GSV_BWD(3, true); break;
+        case 8: GSV_BWD(4, false); break;
+        case 9: GSV_BWD(4, true); break;
         default: return cudaErrorInvalidValue;
     }
-    profile_mark(kProfBackwardGauss, true, stream);
 #undef GSV_BWD
+    profile_mark(kProfBackwardGauss, true, stream);
     count_launches(3);
     return cudaGetLastError();
 }
@@ -772,7 +1023,7 @@ cudaError_t launch_vox_backward_voxel(const Geom &g, int C, int n,
     const float2 *cq = reinterpret_cast<const float2 *>(conics);
     const unsigned grid = (unsigned)ntiles;
 #define GSV_BWDV(Cc)                                                         \
-    vox_bwd_voxel_kernel<Cc><<<grid, kFwdThreads, 0, stream>>>(              \
+    vox_bwd_voxel_kernel<Cc><<<grid, kVoxThreads, 0, stream>>>(              \
         g, bins, ids, rec, cq, grad, pos_grad, conic_grad, int_grad)
     profile_mark(kProfBackwardVoxel, false, stream);
     switch (C) {

@@ -232,6 +232,52 @@ GSV_API int gsv_voxelize_backward_per_gaussian_slab(
     float *pos3d_grad_out, float *conics_grad_out, float *intensities_grad_out,
     void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * L1 loss, standalone: loss_out[0] = sum |vol - target| / denom (one float
+ * in device memory), and its gradient grad_vol = sign(vol - target) *
+ * grad_loss[0] / denom (grad_loss: one float in device memory, the incoming
+ * gradient of the loss). Deterministic reduction. No reference counterpart:
+ * the reference leaves losses to PyTorch in its callers.
+ */
+GSV_API size_t gsv_l1_loss_workspace_bytes(int64_t n);
+
+GSV_API int gsv_l1_loss_forward(int64_t n, const float *vol,
+                                const float *target, float denom,
+                                float *loss_out, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
+GSV_API int gsv_l1_loss_backward(int64_t n, const float *vol,
+                                 const float *target, const float *grad_loss,
+                                 float denom, float *grad_vol, void *stream);
+
+/*
+ * Voxelization with the L1 loss fused in (z-slab form; the full volume is
+ * tile_z_begin = 0, tile_z_end = ceil(Z/8)). The forward writes the volume
+ * and loss_out[0] = sum |vol - target| / denom; the per-Gaussian backward
+ * forms dL/dvol = sign(out_vol - target) * grad_loss[0] / denom while
+ * staging each tile, so no gradient volume is read or written. Workspace:
+ * gsv_voxelize_slab_workspace_bytes. No reference counterpart (extends
+ * voxelize_forward_torch / voxelize_backward_per_gaussian_torch,
+ * bindings.cu:362 and :589).
+ */
+GSV_API int gsv_voxelize_forward_l1(
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
+    int32_t channels, int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    const float *target, float denom, float *out_vol, float *loss_out,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+GSV_API int gsv_voxelize_backward_per_gaussian_l1(
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
+    int32_t channels, int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    const float *out_vol, const float *target, const float *grad_loss,
+    float denom, float *pos3d_grad_out, float *conics_grad_out,
+    float *intensities_grad_out, void *workspace, size_t workspace_bytes,
+    void *stream);
+
 #ifdef __cplusplus
 }
 #endif

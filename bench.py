@@ -346,7 +346,20 @@ def cpu_baseline(cfg, inputs, budget_s=12.0):
 
 # -------------------------------------------------------------------- main
 
+def emit(line: str):
+    """Write the result line to the original stdout (fd 1 is redirected to
+    stderr while the benchmark runs, so library banners stay off stdout)."""
+    os.write(_STDOUT_FD, (line + "\n").encode())
+
+
+_STDOUT_FD = 1
+
+
 def main():
+    global _STDOUT_FD
+    sys.stdout.flush()
+    _STDOUT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
@@ -368,7 +381,7 @@ def main():
         world = 1
         from oracle import ref_api
         if not ref_api.available():
-            print(json.dumps({"impl": "reference",
+            emit(json.dumps({"impl": "reference",
                               "unavailable": "reference extension not built (oracle/_ref)"}))
             return
 
@@ -480,7 +493,7 @@ def main():
         except Exception as exc:  # reported, not fatal
             out["cpu_baseline"] = {"error": str(exc)}
     if rank == 0:
-        print(json.dumps(out))
+        emit(json.dumps(out))
     if world > 1:
         dist.destroy_process_group()
 

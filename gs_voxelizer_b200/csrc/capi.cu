@@ -100,6 +100,15 @@ int fail(int code, const char *fmt, ...) {
     return code;
 }
 
+}  // namespace
+
+namespace gsv {
+// Lets other translation units report through gsv_last_error().
+void set_last_error(const char *msg) { g_last_error = msg; }
+}  // namespace gsv
+
+namespace {
+
 int cuda_status(cudaError_t err, const char *where) {
     if (err == cudaSuccess) return GSV_OK;
     return fail(GSV_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)err,

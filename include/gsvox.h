@@ -278,6 +278,27 @@ GSV_API int gsv_voxelize_backward_per_gaussian_l1(
     float *intensities_grad_out, void *workspace, size_t workspace_bytes,
     void *stream);
 
+/*
+ * Forward voxelization that allocates nothing, for callers that cannot
+ * provide a workspace: code whose device memory belongs to another allocator
+ * (a framework that reserves the GPU's memory up front) or host programs that
+ * receive only ready-made input/output buffers through a foreign-function
+ * interface. Same inputs, output and results as gsv_voxelize_forward; the
+ * per-Gaussian scratch lives in a fixed 16 MiB array inside the library's
+ * device image (held by every GPU that loads the library until exit), so
+ * num_gaussians is limited to 349525 (1-2 channels) or 262144 (3-4
+ * channels); larger inputs return GSV_ERR_WORKSPACE_TOO_SMALL. All calls
+ * share that array: calls that overlap on the GPU race, so serialise them.
+ * The first call on each device resolves the array's address (make it before
+ * any stream capture). No counterpart in the reference.
+ */
+GSV_API int gsv_voxelize_forward_noalloc(
+    const int32_t vol_size_voxel[3], int32_t channels,
+    int32_t num_gaussians, int64_t num_intersects,
+    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const float *pos3d_radii, const float *conics, const float *intensities,
+    float *out_vol, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -153,44 +153,84 @@ __device__ __forceinline__ void fma_if_valid(float &acc, float I, float a,
     }
 }
 
-template <int C>
-__device__ __forceinline__ void fwd_column_pair(
-    const float4 &r0, const float4 &r1, const float4 &r2,
-    const float (&dz)[8], const float (&I)[C], float fx, float fy,
-    bool check_sign, float (&acc)[2][8][C]) {
-    const float thr = r0.w;
-    const float dx = r0.x - fx;
-    const float dy0 = r0.y - fy;
-    const float dy1 = dy0 - 4.f;
-    const float Adx = r1.x * dx, Edx = r2.x * dx;
-    const float P0 = fmaf(dx, fmaf(r1.w, dy0, Adx), r1.y * dy0 * dy0);
-    const float L0 = fmaf(r2.y, dy0, Edx);
-    const float P1 = fmaf(dx, fmaf(r1.w, dy1, Adx), r1.y * dy1 * dy1);
-    const float L1 = fmaf(r2.y, dy1, Edx);
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+
+// sigma (log2 units) of the lane's two columns at z-offset dz:
+// s = P + dz * (L + Cz * dz), evaluated as paired FP32 FMAs (FFMA2).
+__device__ __forceinline__ float2 sigma_pair(float2 P, float2 L, float Cz,
+                                             float dz) {
+    const float2 d = f2(dz);
+    return __ffma2_rn(d, __ffma2_rn(f2(Cz), d, L), P);
+}
+
+template <int C, bool CHECK_SIGN>
+__device__ __forceinline__ void fwd_accumulate(float (&acc)[2][8][C], int j,
+                                               const float (&I)[C], float a0,
+                                               float a1, float s0, float s1,
+                                               float thr) {
+    if (C == 1) {
+        fma_if_valid<CHECK_SIGN>(acc[0][j][0], I[0], a0, s0, thr);
+        fma_if_valid<CHECK_SIGN>(acc[1][j][0], I[0], a1, s1, thr);
+    } else {
+        bool ok0 = s0 >= thr, ok1 = s1 >= thr;
+        if (CHECK_SIGN) {
+            ok0 &= s0 <= 0.f;
+            ok1 &= s1 <= 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            if (ok0) acc[0][j][c] = fmaf(I[c], a0, acc[0][j][c]);
+            if (ok1) acc[1][j][c] = fmaf(I[c], a1, acc[1][j][c]);
+        }
+    }
+}
+
+// One exponential per evaluation.
+template <int C, bool CHECK_SIGN>
+__device__ __forceinline__ void fwd_pair_direct(float2 P, float2 L, float Cz,
+                                                float thr,
+                                                const float (&dz)[8],
+                                                const float (&I)[C],
+                                                float (&acc)[2][8][C]) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const float s0 = fmaf(dz[j], fmaf(r1.z, dz[j], L0), P0);
-        const float s1 = fmaf(dz[j], fmaf(r1.z, dz[j], L1), P1);
-        const float a0 = ex2(s0), a1 = ex2(s1);
-        if (C == 1) {
-            if (check_sign) {
-                fma_if_valid<true>(acc[0][j][0], I[0], a0, s0, thr);
-                fma_if_valid<true>(acc[1][j][0], I[0], a1, s1, thr);
-            } else {
-                fma_if_valid<false>(acc[0][j][0], I[0], a0, s0, thr);
-                fma_if_valid<false>(acc[1][j][0], I[0], a1, s1, thr);
-            }
-        } else {
-            bool ok0 = s0 >= thr, ok1 = s1 >= thr;
-            if (check_sign) {
-                ok0 &= s0 <= 0.f;
-                ok1 &= s1 <= 0.f;
-            }
+        const float2 s = sigma_pair(P, L, Cz, dz[j]);
+        fwd_accumulate<C, CHECK_SIGN>(acc, j, I, ex2(s.x), ex2(s.y), s.x, s.y,
+                                      thr);
+    }
+}
+
+// Exponentials by recurrence along z. With dz_{j+1} = dz_j - 1 the exponent
+// steps by D_j = s_{j+1} - s_j and D_{j+1} = D_j + 2 Cz, so
+//   alpha_{j+1} = alpha_j * r_j,  r_{j+1} = r_j * q,  q = 2^(2 Cz).
+// Two anchors (j = 0 and j = 4) each start a 4-point chain: 4 ex2 per 8
+// voxels instead of 8. Only used when |Cz| <= 2 and thr >= -40: then any
+// point of a chain above the cull threshold implies the chain's anchor
+// exponent is >= -112 (concave quadratic, slope <= 2 sqrt(40 |Cz|)), so the
+// anchor never flushes to zero while a later point still counts, and the
+// products stay within ~10 ulp of the direct exponential. The cull test
+// compares alpha against athr = 2^thr.
+template <int C>
+__device__ __forceinline__ void fwd_pair_chain(float2 P, float2 L, float Cz,
+                                               float q, float athr,
+                                               const float (&dz)[8],
+                                               const float (&I)[C],
+                                               float (&acc)[2][8][C]) {
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-                if (ok0) acc[0][j][c] = fmaf(I[c], a0, acc[0][j][c]);
-                if (ok1) acc[1][j][c] = fmaf(I[c], a1, acc[1][j][c]);
+    for (int seg = 0; seg < 8; seg += 4) {
+        const float2 s0 = sigma_pair(P, L, Cz, dz[seg]);
+        const float2 s1 = sigma_pair(P, L, Cz, dz[seg + 1]);
+        const float2 d = __ffma2_rn(s0, f2(-1.f), s1);
+        float2 a = make_float2(ex2(s0.x), ex2(s0.y));
+        float2 r = make_float2(ex2(d.x), ex2(d.y));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (k > 0) {
+                a = __fmul2_rn(a, r);
+                if (k < 3) r = __fmul2_rn(r, f2(q));
             }
+            fwd_accumulate<C, false>(acc, seg + k, I, a.x, a.y, a.x, a.y,
+                                     athr);
         }
     }
 }
@@ -204,7 +244,7 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                float *__restrict__ out, const float *__restrict__ target,
                float *__restrict__ tile_loss) {
     constexpr int R = Rec<C>::kF4;
-    constexpr int RS = R + 2;  // record + 8 dz
+    constexpr int RS = R + 3;  // record + 8 dz + (q, athr, fast)
     constexpr int kStage = (kFwdBatch * RS * 4 > kTileVoxels * C)
                                ? kFwdBatch * RS * 4
                                : kTileVoxels * C;
@@ -243,6 +283,11 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                                          r0.z - 3.5f);
             sb[k * RS + R + 1] = make_float4(r0.z - 4.5f, r0.z - 5.5f,
                                              r0.z - 6.5f, r0.z - 7.5f);
+            const float Cz = sb[k * RS + 1].z, thr = r0.w;
+            const bool fast = robust_flag(thr) && Cz >= -2.f && thr >= -40.f &&
+                              thr <= 128.f;
+            sb[k * RS + R + 2] =
+                make_float4(ex2(2.f * Cz), ex2(thr), fast ? 1.f : 0.f, 0.f);
         }
         __syncwarp();
 #pragma unroll 1
@@ -252,13 +297,23 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
             const float4 r2 = sb[t * RS + 2];
             const float4 r3 = (R == 4) ? sb[t * RS + 3] : r2;
             const float4 za = sb[t * RS + R], zb = sb[t * RS + R + 1];
+            const float4 ex = sb[t * RS + R + 2];
             const float dz[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
             float I[C];
             record_intensity<C>(r2, r3, I);
-            if (robust_flag(r0.w))
-                fwd_column_pair<C>(r0, r1, r2, dz, I, fx, fy, false, acc);
+            // P, L of the columns (x, y) and (x, y + 4), as pairs
+            const float dx = r0.x - fx;
+            const float2 dy = make_float2(r0.y - fy, r0.y - fy - 4.f);
+            const float2 P = __ffma2_rn(
+                f2(dx), __ffma2_rn(f2(r1.w), dy, f2(r1.x * dx)),
+                __fmul2_rn(__fmul2_rn(f2(r1.y), dy), dy));
+            const float2 L = __ffma2_rn(f2(r2.y), dy, f2(r2.x * dx));
+            if (ex.z != 0.f)
+                fwd_pair_chain<C>(P, L, r1.z, ex.x, ex.y, dz, I, acc);
+            else if (robust_flag(r0.w))
+                fwd_pair_direct<C, false>(P, L, r1.z, r0.w, dz, I, acc);
             else
-                fwd_column_pair<C>(r0, r1, r2, dz, I, fx, fy, true, acc);
+                fwd_pair_direct<C, true>(P, L, r1.z, r0.w, dz, I, acc);
         }
     }
 
@@ -386,11 +441,18 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
             for (int q = 0; q < 8 * C; ++q)
                 v[q] = v[q] > 0.f ? scale : (v[q] < 0.f ? -scale : 0.f);
         }
+        if (C == 1) {
+            // [y][x/2][z][2]: one 16-byte load gives (x, x+1) pairs at z, z+1
 #pragma unroll
-        for (int x = 0; x < 8; ++x)
+            for (int x = 0; x < 8; ++x)
+                buf[yl * S::kRow + (x >> 1) * 16 + zl * 2 + (x & 1)] = v[x];
+        } else {
 #pragma unroll
-            for (int c = 0; c < C; ++c)
-                buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
+            for (int x = 0; x < 8; ++x)
+#pragma unroll
+                for (int c = 0; c < C; ++c)
+                    buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
+        }
     }
 }
 
@@ -480,6 +542,91 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
     return r;
 }
 
+// One y-row for one Gaussian, single channel: the row's 8 columns are taken
+// as 4 column pairs (x, x+1) evaluated with paired FP32 instructions. CHAIN:
+// exponentials by the z recurrence of fwd_pair_chain (two anchors per
+// column); else one ex2 per evaluation. The cull test zeroes w per element,
+// then the moment updates run paired.
+template <bool CHAIN, bool CHECK_SIGN>
+__device__ __forceinline__ RowSums bwd_row_pair(
+    const float *rowbase, float mx, float thr, float athr, float q, float A,
+    float Cz, float E, float Dy, float By2, float Fy, const float2 (&dzp)[8]) {
+    float2 R0 = f2(0.f), R1 = R0, R2 = R0, Rx0 = R0, Rxx = R0, Rx1 = R0;
+#pragma unroll
+    for (int xp = 0; xp < 4; ++xp) {
+        const float2 dx = make_float2(mx - ((float)(2 * xp) + 0.5f),
+                                      mx - ((float)(2 * xp) + 1.5f));
+        const float2 P = __ffma2_rn(dx, __ffma2_rn(f2(A), dx, f2(Dy)), f2(By2));
+        const float2 L = __ffma2_rn(f2(E), dx, f2(Fy));
+        float2 gp[8];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 t =
+                reinterpret_cast<const float4 *>(rowbase + xp * 16)[q4];
+            gp[2 * q4] = make_float2(t.x, t.y);
+            gp[2 * q4 + 1] = make_float2(t.z, t.w);
+        }
+        float2 T0 = f2(0.f), T1 = T0, T2 = T0;
+        auto update = [&](int j, float2 a, bool ok0, bool ok1) {
+            float2 w = __fmul2_rn(a, gp[j]);
+            w.x = ok0 ? w.x : 0.f;
+            w.y = ok1 ? w.y : 0.f;
+            T0 = __fadd2_rn(T0, w);
+            const float2 u = __fmul2_rn(w, dzp[j]);
+            T1 = __fadd2_rn(T1, u);
+            T2 = __ffma2_rn(u, dzp[j], T2);
+        };
+        if (CHAIN) {
+#pragma unroll
+            for (int seg = 0; seg < 8; seg += 4) {
+                const float2 s0 =
+                    __ffma2_rn(dzp[seg], __ffma2_rn(f2(Cz), dzp[seg], L), P);
+                const float2 s1 = __ffma2_rn(
+                    dzp[seg + 1], __ffma2_rn(f2(Cz), dzp[seg + 1], L), P);
+                const float2 d = __ffma2_rn(s0, f2(-1.f), s1);
+                float2 a = make_float2(ex2(s0.x), ex2(s0.y));
+                float2 r = make_float2(ex2(d.x), ex2(d.y));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (k > 0) {
+                        a = __fmul2_rn(a, r);
+                        if (k < 3) r = __fmul2_rn(r, f2(q));
+                    }
+                    update(seg + k, a, a.x >= athr, a.y >= athr);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float2 sv =
+                    __ffma2_rn(dzp[j], __ffma2_rn(f2(Cz), dzp[j], L), P);
+                const float2 a = make_float2(ex2(sv.x), ex2(sv.y));
+                bool ok0 = sv.x >= thr, ok1 = sv.y >= thr;
+                if (CHECK_SIGN) {
+                    ok0 &= sv.x <= 0.f;
+                    ok1 &= sv.y <= 0.f;
+                }
+                update(j, a, ok0, ok1);
+            }
+        }
+        R0 = __fadd2_rn(R0, T0);
+        R1 = __fadd2_rn(R1, T1);
+        R2 = __fadd2_rn(R2, T2);
+        const float2 U = __fmul2_rn(dx, T0);
+        Rx0 = __fadd2_rn(Rx0, U);
+        Rxx = __ffma2_rn(U, dx, Rxx);
+        Rx1 = __ffma2_rn(dx, T1, Rx1);
+    }
+    RowSums r;
+    r.R0 = R0.x + R0.y;
+    r.R1 = R1.x + R1.y;
+    r.R2 = R2.x + R2.y;
+    r.Rx0 = Rx0.x + Rx0.y;
+    r.Rxx = Rxx.x + Rxx.y;
+    r.Rx1 = Rx1.x + Rx1.y;
+    return r;
+}
+
 template <int C, bool LOSS>
 __global__ void __launch_bounds__(kBwdWarps * 32, C <= 2 ? 6 : 4)
 vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
@@ -548,11 +695,20 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
         const float thr = r0.w;
         const bool all_robust = __all_sync(0xffffffffu, robust_flag(thr));
         float dz[8], dz2[8];
+        float2 dzp[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             dz[j] = r0.z - ((float)j + 0.5f);
             dz2[j] = dz[j] * dz[j];
+            dzp[j] = f2(dz[j]);
         }
+        // chain eligibility (see fwd_pair_chain); invalid lanes do not veto
+        const bool lane_fast = robust_flag(thr) && r1.z >= -2.f &&
+                               thr >= -40.f && thr <= 128.f;
+        const bool all_fast =
+            C == 1 && __all_sync(0xffffffffu, lane_fast || !valid);
+        const float athr = valid ? ex2(thr) : __int_as_float(0x7fc00000);
+        const float qz = ex2(2.f * r1.z);
 
         // sums over the Gaussian's voxels of w-weighted monomials of d, where
         // w = alpha * h and h = sum_c I_c dL/dvol_c (C > 1) or dL/dvol (C = 1)
@@ -568,12 +724,26 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
             const float dy = r0.y - ((float)yl + 0.5f);
             const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
             const float *colbase = buf + yl * S::kRow;
-            const RowSums rs =
-                all_robust
-                    ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
-                                        Dy, By2, Fy, dz, dz2, I, W)
-                    : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
-                                       Dy, By2, Fy, dz, dz2, I, W);
+            RowSums rs;
+            if (C == 1) {
+                rs = all_fast
+                         ? bwd_row_pair<true, false>(colbase, r0.x, thr, athr,
+                                                     qz, r1.x, r1.z, r2.x, Dy,
+                                                     By2, Fy, dzp)
+                         : (all_robust
+                                ? bwd_row_pair<false, false>(
+                                      colbase, r0.x, thr, athr, qz, r1.x, r1.z,
+                                      r2.x, Dy, By2, Fy, dzp)
+                                : bwd_row_pair<false, true>(
+                                      colbase, r0.x, thr, athr, qz, r1.x, r1.z,
+                                      r2.x, Dy, By2, Fy, dzp));
+            } else {
+                rs = all_robust
+                         ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z,
+                                             r2.x, Dy, By2, Fy, dz, dz2, I, W)
+                         : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z,
+                                            r2.x, Dy, By2, Fy, dz, dz2, I, W);
+            }
             if (C == 1) W[0] += rs.R0;  // intensity grad = sum(w) (C = 1)
             Sxx += rs.Rxx;
             Szz += rs.R2;

@@ -51,7 +51,7 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       cudaStream_t stream,
                                       const float *target,
                                       const float *grad_loss,
-                                      float inv_denom);
+                                      float inv_denom, int stage);
 size_t l1_workspace_bytes(long long n);
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
@@ -245,12 +245,18 @@ int backward_impl(const char *fn, bool per_gaussian, const gsv::Geom &g,
                                              con, inten, grad, pos_grad,
                                              con_grad, int_grad, ws,
                                              as_stream(stream), nullptr,
-                                             nullptr, 1.f)
+                                             nullptr, 1.f, gsv::kBwdFull)
             : gsv::launch_vox_backward_voxel(g, C, n, nisect, ids, bins, pos,
                                              con, inten, grad, pos_grad,
                                              con_grad, int_grad, ws,
                                              as_stream(stream));
     return cuda_status(err, fn);
+}
+
+// Binning part of the fused-L1 workspace (256-byte aligned).
+size_t l1_bin_part(const gsv::Geom &g, long long nisect) {
+    return (gsv::bin_workspace_bytes(g.slab_tiles(), nisect) + 255) &
+           ~size_t(255);
 }
 
 }  // namespace
@@ -503,39 +509,78 @@ int gsv_l1_loss_backward(int64_t n, const float *vol, const float *target,
                        fn);
 }
 
+size_t gsv_voxelize_l1_workspace_bytes(int32_t n, int32_t C, int64_t nisect,
+                                       const int32_t vol[3], int32_t tz0,
+                                       int32_t tz1) {
+    if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
+    if (C < 1 || C > 4) return 0;
+    const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
+    if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
+    const long long ni = nisect < 0 ? 0 : nisect;
+    return l1_bin_part(g, ni) +
+           gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(), ni);
+}
+
 int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
                             int32_t C, int32_t n, int64_t nisect,
-                            const int32_t *ids, const int32_t *bins,
+                            const int32_t *tile_min, const int32_t *tile_max,
                             const float *pos, const float *con,
                             const float *inten, const float *target,
-                            float denom, float *out, float *loss_out,
-                            void *ws, size_t ws_bytes, void *stream) {
+                            float denom, int32_t *ids_out, int32_t *bins_out,
+                            float *out, float *loss_out, void *ws,
+                            size_t ws_bytes, void *stream) {
     const char *fn = "gsv_voxelize_forward_l1";
     if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
     const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
     if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
-    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
-                               ws_bytes, ws);
-    if (st) return st;
+    GSV_REQUIRE(C >= 1 && C <= 4, GSV_ERR_UNSUPPORTED_CHANNELS,
+                "%s: %d channels requested, 1..4 supported", fn, C);
+    GSV_REQUIRE(n >= 0 && nisect >= 0, GSV_ERR_INVALID_ARGUMENT,
+                "%s: negative size", fn);
+    GSV_REQUIRE(nisect <= INT32_MAX && g.slab_tiles() <= INT32_MAX,
+                GSV_ERR_SIZE_OVERFLOW, "%s: sizes exceed int32", fn);
+    const size_t need = gsv_voxelize_l1_workspace_bytes(n, C, nisect, vol,
+                                                        tz0, tz1);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
+                need);
     const long long nvox =
         (long long)(g.z_end() - g.z_begin()) * g.Y * g.X * C;
     GSV_REQUIRE((out && target) || nvox == 0, GSV_ERR_INVALID_ARGUMENT,
                 "%s: out_vol or target is null", fn);
     GSV_REQUIRE(loss_out && denom != 0.f, GSV_ERR_INVALID_ARGUMENT,
                 "%s: loss_out is null or denom is 0", fn);
+    GSV_REQUIRE(g.slab_tiles() == 0 || bins_out, GSV_ERR_INVALID_ARGUMENT,
+                "%s: tile_bins is null", fn);
+    GSV_REQUIRE(nisect == 0 || (ids_out && tile_min && tile_max && pos && con &&
+                                inten),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
     cudaStream_t s = as_stream(stream);
+    char *bin_ws = static_cast<char *>(ws);
+    char *vox_ws = bin_ws + l1_bin_part(g, nisect);
+    gsv::enable_large_smem();
+    cudaError_t err = gsv::launch_binning(n, nisect, tile_min, tile_max, g.Tx,
+                                          g.Ty, g.tz0, g.tz1, ids_out, bins_out,
+                                          bin_ws, s);
+    if (err) return cuda_status(err, fn);
     if (nisect == 0) {
         // empty volume: loss = sum |target| / denom
-        cudaError_t err = cudaMemsetAsync(out, 0, sizeof(float) * nvox, s);
+        err = cudaMemsetAsync(out, 0, sizeof(float) * nvox, s);
         if (err) return cuda_status(err, fn);
         return cuda_status(gsv::launch_empty_l1(nvox, target,
                                                 1.0 / (double)denom, loss_out,
-                                                ws, s),
+                                                vox_ws, s),
                            fn);
     }
-    return cuda_status(gsv::launch_vox_forward(g, C, n, ids, bins, pos, con,
-                                               inten, out, ws, s, target,
-                                               loss_out, 1.0 / (double)denom),
+    err = gsv::launch_vox_forward(g, C, n, ids_out, bins_out, pos, con, inten,
+                                  out, vox_ws, s, target, loss_out,
+                                  1.0 / (double)denom);
+    if (err) return cuda_status(err, fn);
+    // plan the backward's work queue now, while the tile ranges are at hand
+    return cuda_status(gsv::launch_vox_backward_gauss(
+                           g, C, n, nisect, ids_out, bins_out, pos, con, inten,
+                           out, nullptr, nullptr, nullptr, vox_ws, s, target,
+                           nullptr, 1.f, gsv::kBwdPlanOnly),
                        fn);
 }
 
@@ -550,18 +595,27 @@ int gsv_voxelize_backward_per_gaussian_l1(
     if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
     const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
     if (!check_slab(g, fn)) return GSV_ERR_INVALID_ARGUMENT;
-    int st = vox_common_checks(fn, g, C, n, nisect, ids, bins, pos, con, inten,
-                               ws_bytes, ws);
-    if (st) return st;
+    GSV_REQUIRE(C >= 1 && C <= 4, GSV_ERR_UNSUPPORTED_CHANNELS,
+                "%s: %d channels requested, 1..4 supported", fn, C);
+    GSV_REQUIRE(n >= 0 && nisect >= 0 && nisect <= INT32_MAX,
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes", fn);
+    const size_t need = gsv_voxelize_l1_workspace_bytes(n, C, nisect, vol,
+                                                        tz0, tz1);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
+                need);
     GSV_REQUIRE(n == 0 || (pos_grad && con_grad && int_grad),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null gradient output", fn);
-    GSV_REQUIRE(nisect == 0 || (out_vol && target && grad_loss),
-                GSV_ERR_INVALID_ARGUMENT, "%s: null volume input", fn);
+    GSV_REQUIRE(nisect == 0 || (ids && bins && pos && con && inten && out_vol &&
+                                target && grad_loss),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
     GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
+    char *vox_ws = static_cast<char *>(ws) + l1_bin_part(g, nisect);
     return cuda_status(gsv::launch_vox_backward_gauss(
                            g, C, n, nisect, ids, bins, pos, con, inten,
-                           out_vol, pos_grad, con_grad, int_grad, ws,
-                           as_stream(stream), target, grad_loss, 1.f / denom),
+                           out_vol, pos_grad, con_grad, int_grad, vox_ws,
+                           as_stream(stream), target, grad_loss, 1.f / denom,
+                           gsv::kBwdPrepared),
                        fn);
 }
 

@@ -46,6 +46,11 @@ inline Geom make_geom(const int32_t vol_zyx[3], int tz0 = 0, int tz1 = -1) {
 // Running count of kernels this library has launched (gsv_launch_count()).
 void count_launches(int k);
 
+// Stages of launch_vox_backward_gauss: everything; only the work plan (the
+// forward already built the records in the workspace); only the kernel (a
+// previous kBwdPlanOnly call prepared the workspace).
+enum BwdStage { kBwdFull = 0, kBwdPlanOnly = 1, kBwdPrepared = 2 };
+
 // Optional CUDA events recorded right before / after the main voxelization
 // kernels (gsv_profile_kernel()); no-ops unless a caller installed events.
 enum ProfKind { kProfForward = 0, kProfBackwardGauss = 1, kProfBackwardVoxel = 2 };

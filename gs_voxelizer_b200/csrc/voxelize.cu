@@ -441,18 +441,11 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
             for (int q = 0; q < 8 * C; ++q)
                 v[q] = v[q] > 0.f ? scale : (v[q] < 0.f ? -scale : 0.f);
         }
-        if (C == 1) {
-            // [y][x/2][z][2]: one 16-byte load gives (x, x+1) pairs at z, z+1
 #pragma unroll
-            for (int x = 0; x < 8; ++x)
-                buf[yl * S::kRow + (x >> 1) * 16 + zl * 2 + (x & 1)] = v[x];
-        } else {
+        for (int x = 0; x < 8; ++x)
 #pragma unroll
-            for (int x = 0; x < 8; ++x)
-#pragma unroll
-                for (int c = 0; c < C; ++c)
-                    buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
-        }
+            for (int c = 0; c < C; ++c)
+                buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
     }
 }
 
@@ -542,91 +535,6 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
     return r;
 }
 
-// One y-row for one Gaussian, single channel: the row's 8 columns are taken
-// as 4 column pairs (x, x+1) evaluated with paired FP32 instructions. CHAIN:
-// exponentials by the z recurrence of fwd_pair_chain (two anchors per
-// column); else one ex2 per evaluation. The cull test zeroes w per element,
-// then the moment updates run paired.
-template <bool CHAIN, bool CHECK_SIGN>
-__device__ __forceinline__ RowSums bwd_row_pair(
-    const float *rowbase, float mx, float thr, float athr, float q, float A,
-    float Cz, float E, float Dy, float By2, float Fy, const float2 (&dzp)[8]) {
-    float2 R0 = f2(0.f), R1 = R0, R2 = R0, Rx0 = R0, Rxx = R0, Rx1 = R0;
-#pragma unroll
-    for (int xp = 0; xp < 4; ++xp) {
-        const float2 dx = make_float2(mx - ((float)(2 * xp) + 0.5f),
-                                      mx - ((float)(2 * xp) + 1.5f));
-        const float2 P = __ffma2_rn(dx, __ffma2_rn(f2(A), dx, f2(Dy)), f2(By2));
-        const float2 L = __ffma2_rn(f2(E), dx, f2(Fy));
-        float2 gp[8];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 t =
-                reinterpret_cast<const float4 *>(rowbase + xp * 16)[q4];
-            gp[2 * q4] = make_float2(t.x, t.y);
-            gp[2 * q4 + 1] = make_float2(t.z, t.w);
-        }
-        float2 T0 = f2(0.f), T1 = T0, T2 = T0;
-        auto update = [&](int j, float2 a, bool ok0, bool ok1) {
-            float2 w = __fmul2_rn(a, gp[j]);
-            w.x = ok0 ? w.x : 0.f;
-            w.y = ok1 ? w.y : 0.f;
-            T0 = __fadd2_rn(T0, w);
-            const float2 u = __fmul2_rn(w, dzp[j]);
-            T1 = __fadd2_rn(T1, u);
-            T2 = __ffma2_rn(u, dzp[j], T2);
-        };
-        if (CHAIN) {
-#pragma unroll
-            for (int seg = 0; seg < 8; seg += 4) {
-                const float2 s0 =
-                    __ffma2_rn(dzp[seg], __ffma2_rn(f2(Cz), dzp[seg], L), P);
-                const float2 s1 = __ffma2_rn(
-                    dzp[seg + 1], __ffma2_rn(f2(Cz), dzp[seg + 1], L), P);
-                const float2 d = __ffma2_rn(s0, f2(-1.f), s1);
-                float2 a = make_float2(ex2(s0.x), ex2(s0.y));
-                float2 r = make_float2(ex2(d.x), ex2(d.y));
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    if (k > 0) {
-                        a = __fmul2_rn(a, r);
-                        if (k < 3) r = __fmul2_rn(r, f2(q));
-                    }
-                    update(seg + k, a, a.x >= athr, a.y >= athr);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float2 sv =
-                    __ffma2_rn(dzp[j], __ffma2_rn(f2(Cz), dzp[j], L), P);
-                const float2 a = make_float2(ex2(sv.x), ex2(sv.y));
-                bool ok0 = sv.x >= thr, ok1 = sv.y >= thr;
-                if (CHECK_SIGN) {
-                    ok0 &= sv.x <= 0.f;
-                    ok1 &= sv.y <= 0.f;
-                }
-                update(j, a, ok0, ok1);
-            }
-        }
-        R0 = __fadd2_rn(R0, T0);
-        R1 = __fadd2_rn(R1, T1);
-        R2 = __fadd2_rn(R2, T2);
-        const float2 U = __fmul2_rn(dx, T0);
-        Rx0 = __fadd2_rn(Rx0, U);
-        Rxx = __ffma2_rn(U, dx, Rxx);
-        Rx1 = __ffma2_rn(dx, T1, Rx1);
-    }
-    RowSums r;
-    r.R0 = R0.x + R0.y;
-    r.R1 = R1.x + R1.y;
-    r.R2 = R2.x + R2.y;
-    r.Rx0 = Rx0.x + Rx0.y;
-    r.Rxx = Rxx.x + Rxx.y;
-    r.Rx1 = Rx1.x + Rx1.y;
-    return r;
-}
-
 template <int C, bool LOSS>
 __global__ void __launch_bounds__(kBwdWarps * 32, C <= 2 ? 6 : 4)
 vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
@@ -695,20 +603,11 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
         const float thr = r0.w;
         const bool all_robust = __all_sync(0xffffffffu, robust_flag(thr));
         float dz[8], dz2[8];
-        float2 dzp[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             dz[j] = r0.z - ((float)j + 0.5f);
             dz2[j] = dz[j] * dz[j];
-            dzp[j] = f2(dz[j]);
         }
-        // chain eligibility (see fwd_pair_chain); invalid lanes do not veto
-        const bool lane_fast = robust_flag(thr) && r1.z >= -2.f &&
-                               thr >= -40.f && thr <= 128.f;
-        const bool all_fast =
-            C == 1 && __all_sync(0xffffffffu, lane_fast || !valid);
-        const float athr = valid ? ex2(thr) : __int_as_float(0x7fc00000);
-        const float qz = ex2(2.f * r1.z);
 
         // sums over the Gaussian's voxels of w-weighted monomials of d, where
         // w = alpha * h and h = sum_c I_c dL/dvol_c (C > 1) or dL/dvol (C = 1)
@@ -724,26 +623,12 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
             const float dy = r0.y - ((float)yl + 0.5f);
             const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
             const float *colbase = buf + yl * S::kRow;
-            RowSums rs;
-            if (C == 1) {
-                rs = all_fast
-                         ? bwd_row_pair<true, false>(colbase, r0.x, thr, athr,
-                                                     qz, r1.x, r1.z, r2.x, Dy,
-                                                     By2, Fy, dzp)
-                         : (all_robust
-                                ? bwd_row_pair<false, false>(
-                                      colbase, r0.x, thr, athr, qz, r1.x, r1.z,
-                                      r2.x, Dy, By2, Fy, dzp)
-                                : bwd_row_pair<false, true>(
-                                      colbase, r0.x, thr, athr, qz, r1.x, r1.z,
-                                      r2.x, Dy, By2, Fy, dzp));
-            } else {
-                rs = all_robust
-                         ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z,
-                                             r2.x, Dy, By2, Fy, dz, dz2, I, W)
-                         : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z,
-                                            r2.x, Dy, By2, Fy, dz, dz2, I, W);
-            }
+            const RowSums rs =
+                all_robust
+                    ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
+                                        Dy, By2, Fy, dz, dz2, I, W)
+                    : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
+                                       Dy, By2, Fy, dz, dz2, I, W);
             if (C == 1) W[0] += rs.R0;  // intensity grad = sum(w) (C = 1)
             Sxx += rs.Rxx;
             Szz += rs.R2;
@@ -958,6 +843,23 @@ vox_bwd_voxel_kernel(Geom g, const int2 *__restrict__ bins,
     }
 }
 
+// Zeroes the three gradient arrays and the work counter in one launch.
+__global__ void __launch_bounds__(256)
+zero_grads_kernel(int n, int C, float *__restrict__ pos_grad,
+                  float *__restrict__ conic_grad, float *__restrict__ int_grad,
+                  int *__restrict__ counter) {
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    if (tid < 4) counter[tid] = 0;
+    for (long long i = tid; i < n; i += stride) {
+        reinterpret_cast<float4 *>(pos_grad)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float2 *>(conic_grad)[3 * i + 0] = make_float2(0.f, 0.f);
+        reinterpret_cast<float2 *>(conic_grad)[3 * i + 1] = make_float2(0.f, 0.f);
+        reinterpret_cast<float2 *>(conic_grad)[3 * i + 2] = make_float2(0.f, 0.f);
+        for (int c = 0; c < C; ++c) int_grad[i * C + c] = 0.f;
+    }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------ host launchers
@@ -1106,6 +1008,23 @@ static void bwd_launch(cudaStream_t stream, const Geom &g, const int2 *bins,
         conic_grad, int_grad, target, grad_loss, inv_denom);
 }
 
+// Backward work plan from tile_bins: per-tile bucket counts, their scan and
+// the bucket -> tile map (the kernel's work queue).
+static cudaError_t launch_bwd_plan(const int2 *bins, long long ntiles,
+                                   int *item_counts, long long *partials,
+                                   int *item_bins, int *item_tile,
+                                   cudaStream_t stream) {
+    const unsigned tblocks = (unsigned)((ntiles + 255) / 256);
+    item_count_kernel<<<tblocks, 256, 0, stream>>>(bins, ntiles, item_counts);
+    cudaError_t err = scan_counts_to_bins(item_counts, ntiles, partials,
+                                          item_bins, stream);
+    if (err) return err;
+    item_fill_kernel<<<tblocks, 256, 0, stream>>>(
+        reinterpret_cast<const int2 *>(item_bins), ntiles, item_tile);
+    count_launches(2);
+    return cudaGetLastError();
+}
+
 // target != nullptr: fused L1; `grad` is then the forward volume and
 // dL/dvol = sign(vol - target) * grad_loss[0] * inv_denom.
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
@@ -1119,7 +1038,7 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       cudaStream_t stream,
                                       const float *target,
                                       const float *grad_loss,
-                                      float inv_denom) {
+                                      float inv_denom, int stage) {
     const long long ntiles = g.slab_tiles();
     const VoxLayout L = vox_layout(n, C, ntiles, nisect);
     char *base = static_cast<char *>(ws);
@@ -1132,19 +1051,31 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     const long long nblocks = (ntiles + 4095) / 4096;
 
     cudaError_t err;
-    if ((err = cudaMemsetAsync(pos_grad, 0, sizeof(float) * 4 * (size_t)n, stream))) return err;
-    if ((err = cudaMemsetAsync(conic_grad, 0, sizeof(float) * 6 * (size_t)n, stream))) return err;
-    if ((err = cudaMemsetAsync(int_grad, 0, sizeof(float) * C * (size_t)n, stream))) return err;
-    if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
-    if ((err = cudaMemsetAsync(counter, 0, sizeof(int) * 4, stream))) return err;
-    if ((err = launch_prep(n, C, pos_radii, conics, intens, rec, stream))) return err;
-
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
-    const unsigned tblocks = (unsigned)((ntiles + 255) / 256);
-    item_count_kernel<<<tblocks, 256, 0, stream>>>(bins, ntiles, item_counts);
-    if ((err = scan_counts_to_bins(item_counts, ntiles, partials, item_bins, stream))) return err;
-    item_fill_kernel<<<tblocks, 256, 0, stream>>>(
-        reinterpret_cast<const int2 *>(item_bins), ntiles, item_tile);
+    if (stage == kBwdPlanOnly) {
+        // records were built by the forward in this workspace; only plan
+        if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
+        return launch_bwd_plan(bins, ntiles, item_counts, partials, item_bins,
+                               item_tile, stream);
+    }
+    if (stage == kBwdPrepared) {
+        zero_grads_kernel<<<std::max(1, std::min((n + 255) / 256, kSMs * 8)),
+                            256, 0, stream>>>(n, C, pos_grad, conic_grad,
+                                              int_grad, counter);
+        count_launches(1);
+        if ((err = cudaGetLastError())) return err;
+        if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
+    } else {
+        if ((err = cudaMemsetAsync(pos_grad, 0, sizeof(float) * 4 * (size_t)n, stream))) return err;
+        if ((err = cudaMemsetAsync(conic_grad, 0, sizeof(float) * 6 * (size_t)n, stream))) return err;
+        if ((err = cudaMemsetAsync(int_grad, 0, sizeof(float) * C * (size_t)n, stream))) return err;
+        if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
+        if ((err = cudaMemsetAsync(counter, 0, sizeof(int) * 4, stream))) return err;
+        if ((err = launch_prep(n, C, pos_radii, conics, intens, rec, stream))) return err;
+        if ((err = launch_bwd_plan(bins, ntiles, item_counts, partials,
+                                   item_bins, item_tile, stream)))
+            return err;
+    }
     const long long *total = partials + nblocks;
     const float2 *cq = reinterpret_cast<const float2 *>(conics);
     const int2 *ib = reinterpret_cast<const int2 *>(item_bins);
@@ -1167,7 +1098,7 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     }
 #undef GSV_BWD
     profile_mark(kProfBackwardGauss, true, stream);
-    count_launches(3);
+    count_launches(1);
     return cudaGetLastError();
 }
 

@@ -86,16 +86,24 @@ class _VoxelizeL1(Function):
         if tuple(target.shape) != (*plan.shape, C):
             raise ValueError(f"target shape {tuple(target.shape)} != "
                              f"{(*plan.shape, C)}")
-        ids, bins = plan.bin(tile_min, tile_max)
-        n, n_isect = int(pos3d_radii.shape[0]), int(ids.numel())
+        tile_min, tile_max = tile_min.contiguous(), tile_max.contiguous()
+        n = int(pos3d_radii.shape[0])
+        n_isect = plan.count(tile_min, tile_max)
+        i32 = dict(dtype=torch.int32, device=dev)
+        ids = torch.empty((n_isect,), **i32)
+        bins = torch.empty((plan.num_tiles, 2), **i32)
         out = torch.empty(target.shape, dtype=torch.float32, device=dev)
         loss = torch.empty((), dtype=torch.float32, device=dev)
-        ws = plan._ws(n, C, n_isect, dev)
+        ws = _C._workspace(lib.gsv_voxelize_l1_workspace_bytes(
+            n, C, n_isect, i3(plan.vol), plan.tz0, plan.tz1), dev)
+        # one call: binning, voxelization + loss, backward work plan in ws
         check(lib.gsv_voxelize_forward_l1(
-            i3(plan.vol), plan.tz0, plan.tz1, C, n, n_isect, _C._ptr(ids),
-            _C._ptr(bins), _C._ptr(pos3d_radii), _C._ptr(conics),
-            _C._ptr(intensities), _C._ptr(target), float(denom), _C._ptr(out),
+            i3(plan.vol), plan.tz0, plan.tz1, C, n, n_isect,
+            tile_min.data_ptr(), tile_max.data_ptr(), _C._ptr(pos3d_radii),
+            _C._ptr(conics), _C._ptr(intensities), _C._ptr(target),
+            float(denom), _C._ptr(ids), _C._ptr(bins), _C._ptr(out),
             loss.data_ptr(), ws.data_ptr(), ws.numel(), _C._stream(dev)))
+        ctx.ws = ws
         ctx.plan, ctx.denom, ctx.group, ctx.one_d = plan, float(denom), group, one_d
         ctx.save_for_backward(pos3d_radii, conics, intensities, ids, bins, out,
                               target)
@@ -115,7 +123,7 @@ class _VoxelizeL1(Function):
         if grad_loss is None:
             grad_loss = torch.zeros((), **f)
         grad_loss = grad_loss.contiguous().to(torch.float32)
-        ws = plan._ws(n, C, n_isect, dev)
+        ws = ctx.ws  # records and work plan left by the forward
         check(lib.gsv_voxelize_backward_per_gaussian_l1(
             i3(plan.vol), plan.tz0, plan.tz1, C, n, n_isect, _C._ptr(ids),
             _C._ptr(bins), _C._ptr(pr), _C._ptr(cq), _C._ptr(inten),

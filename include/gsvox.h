@@ -251,21 +251,33 @@ GSV_API int gsv_l1_loss_backward(int64_t n, const float *vol,
                                  float denom, float *grad_vol, void *stream);
 
 /*
- * Voxelization with the L1 loss fused in (z-slab form; the full volume is
- * tile_z_begin = 0, tile_z_end = ceil(Z/8)). The forward writes the volume
- * and loss_out[0] = sum |vol - target| / denom; the per-Gaussian backward
- * forms dL/dvol = sign(out_vol - target) * grad_loss[0] / denom while
- * staging each tile, so no gradient volume is read or written. Workspace:
- * gsv_voxelize_slab_workspace_bytes. No reference counterpart (extends
- * voxelize_forward_torch / voxelize_backward_per_gaussian_torch,
- * bindings.cu:362 and :589).
+ * One training step's voxelization with the L1 loss fused in (z-slab form;
+ * the full volume is tile_z_begin = 0, tile_z_end = ceil(Z/8)), as two calls
+ * sharing one workspace of gsv_voxelize_l1_workspace_bytes:
+ *  - forward: bins the slab's (tile, gaussian) pairs from the tile boxes into
+ *    gaussian_ids_sorted_out / tile_bins_out (as
+ *    gsv_bin_and_sort_gaussians_slab), writes the volume and
+ *    loss_out[0] = sum |vol - target| / denom, and leaves the per-Gaussian
+ *    records and the backward's work plan in the workspace;
+ *  - backward: with the same ids, tile_bins and unchanged workspace, forms
+ *    dL/dvol = sign(out_vol - target) * grad_loss[0] / denom while staging
+ *    each tile (no gradient volume is read or written) and writes the
+ *    per-Gaussian gradients like gsv_voxelize_backward_per_gaussian.
+ * num_intersects: the slab's pair count (gsv_count_slab_intersects).
+ * No reference counterpart (fuses bindings.cu:261, :362 and :589 with the
+ * loss the reference's callers compute in PyTorch).
  */
+GSV_API size_t gsv_voxelize_l1_workspace_bytes(
+    int32_t num_gaussians, int32_t channels, int64_t num_intersects,
+    const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end);
+
 GSV_API int gsv_voxelize_forward_l1(
     const int32_t vol_size_voxel[3], int32_t tile_z_begin, int32_t tile_z_end,
     int32_t channels, int32_t num_gaussians, int64_t num_intersects,
-    const int32_t *gaussian_ids_sorted, const int32_t *tile_bins,
+    const int32_t *tile_min, const int32_t *tile_max,
     const float *pos3d_radii, const float *conics, const float *intensities,
-    const float *target, float denom, float *out_vol, float *loss_out,
+    const float *target, float denom, int32_t *gaussian_ids_sorted_out,
+    int32_t *tile_bins_out, float *out_vol, float *loss_out,
     void *workspace, size_t workspace_bytes, void *stream);
 
 GSV_API int gsv_voxelize_backward_per_gaussian_l1(

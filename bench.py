@@ -307,6 +307,20 @@ def time_main_kernels(step_obj, steps, flush):
     return res
 
 
+def profiled_traffic(kernel: str, workload: str):
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch of the kernel
+    from the committed ncu summary of this workload (profiles/), or None."""
+    name = {"forward": "vox_fwd_kernel", "backward": "vox_bwd_gauss_kernel"}[kernel]
+    path = os.path.join(ROOT, "profiles", f"{name}_{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline(cfg, inputs, budget_s=12.0):
     """The C oracle (oracle/gsv_oracle.c, OpenMP) on a bounded sample of the
     same workload: consecutive 2-tile-layer z-slabs of the volume, fwd + L1 +
@@ -483,7 +497,8 @@ def main():
         out["roofline"] = {
             "bound": "mufu", "kernel": f"voxelize {dom}",
             "achieved": achieved, "peak": peak, "unit": "Geval/s",
-            "frac": achieved / peak, "traffic": None,
+            "frac": achieved / peak,
+            "traffic": profiled_traffic(dom, cfg.name),
             "note": ("one MUFU.EX2 per Gaussian-voxel evaluation at 16/clk/SM "
                      "x 148 SMs x max SM clock; E per launch = this rank's "
                      "forward evaluations")}

@@ -360,6 +360,47 @@ def cpu_baseline(cfg, inputs, budget_s=12.0):
 
 # -------------------------------------------------------------------- main
 
+def sweep_configs(kind):
+    from gs_voxelizer_b200.workloads import count_sweep, volume_sweep
+    if kind == "count":
+        return [count_sweep(n) for n in (10_000, 30_000, 100_000, 300_000, 1_000_000)]
+    return [volume_sweep(e, c) for c in (1, 4) for e in (128, 256, 512, 768)]
+
+
+def run_sweep(args):
+    """Per configuration: fused-L1 step, drop-in step and the reference's
+    extension (when built), fwd / bwd / step ms with CUDA events (median of
+    `steps` after `warmup`), L2 flushed between steps."""
+    from oracle import ref_api
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    steps = max(3, min(args.steps, 10))
+    for cfg in sweep_configs(args.sweep):
+        inputs = make_inputs(cfg, 1)
+        row = {"sweep": args.sweep, "workload": cfg.name, "vol_zyx": list(cfg.vol),
+               "gaussians": cfg.n, "channels": cfg.channels}
+        arms = [("fused", "ours"), ("dropin", "ours")]
+        if ref_api.available():
+            arms.append(("reference", "reference"))
+        for arm, impl in arms:
+            st = Step(impl, cfg, 1, 0, inputs)
+            st.mode = "fused" if arm == "fused" else "dropin"
+            if arm == "fused":
+                E, n_isect = st.evaluations()
+                row["evals_per_pass"] = E
+                row["intersections"] = n_isect
+            for _ in range(max(3, args.warmup)):
+                st.step()
+            torch.cuda.synchronize()
+            fwd, bwd = time_fwd_bwd(st, steps, flush)
+            total, per = time_steps(st.step, steps, flush)
+            step_ms = statistics.median(per)
+            row[arm] = {"fwd_ms": fwd, "bwd_ms": bwd, "step_ms": step_ms,
+                        "evals_per_s": 2 * row["evals_per_pass"] / (step_ms / 1e3)}
+            del st
+            torch.cuda.empty_cache()
+        emit(json.dumps(row))
+
+
 def emit(line: str):
     """Write the result line to the original stdout (fd 1 is redirected to
     stderr while the benchmark runs, so library banners stay off stdout)."""
@@ -382,6 +423,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 128^3, 25k Gaussians, 3 steps")
+    ap.add_argument("--workload", choices=["step256", "shard2048"],
+                    default="step256",
+                    help="step256: BASELINE config 2, weak-scaled over GPUs; "
+                         "shard2048: config 5 (2048^3, 8M Gaussians), the same "
+                         "volume z-slab sharded over the GPUs (strong scaling)")
+    ap.add_argument("--sweep", choices=["count", "volume"], default=None,
+                    help="BASELINE config 3 (Gaussian-count sweep) or 4 "
+                         "(volume x channel sweep): one JSON line per case")
     ap.add_argument("--profile-run", action="store_true",
                     help="only run warmup + steps training steps (for ncu), print no JSON")
     args = ap.parse_args()
@@ -389,8 +438,16 @@ def main():
 
     world, rank, local = setup_dist(args.gpus)
     impl = args.impl
+    if args.sweep:
+        run_sweep(args)
+        return
     if impl == "reference" and rank != 0:
         return  # the reference is single-GPU: rank 0 alone runs it
+    if impl == "reference" and args.workload == "shard2048":
+        emit(json.dumps({"impl": "reference", "unavailable":
+                         "the reference's voxel index is int32 (voxelize.cu:63); "
+                         "a 2048^3 volume overflows it"}))
+        return
     if impl == "reference":
         world = 1
         from oracle import ref_api
@@ -399,12 +456,17 @@ def main():
                               "unavailable": "reference extension not built (oracle/_ref)"}))
             return
 
-    cfg = workload(world)
+    strong = args.workload == "shard2048"
+    if strong:
+        from gs_voxelizer_b200.workloads import CONFIGS
+        cfg = CONFIGS["shard2048"]
+    else:
+        cfg = workload(world)
     if args.small:
         from gs_voxelizer_b200.workloads import Config
         cfg = Config("small128", (128, 128, 128), 25_000, pos=cfg.pos,
                      scale=(0.004, 0.04), intensity=cfg.intensity, ellipsoids=16)
-    inputs = make_inputs(cfg, world)
+    inputs = make_inputs(cfg, 1 if strong else world)
     st = Step(impl, cfg, world, rank, inputs)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     if args.profile_run:
@@ -447,7 +509,7 @@ def main():
     fwd_ms, bwd_ms = max_over_ranks(fwd_ms, world), max_over_ranks(bwd_ms, world)
 
     dropin = None
-    if impl != "reference":
+    if impl != "reference" and not strong:
         # the same step through the reference-compatible API (voxelize_gaussians
         # + torch.nn.functional.l1_loss), as a user switching over unchanged
         st.mode = "dropin"
@@ -460,9 +522,13 @@ def main():
         st.mode = "fused"
 
     out = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": (METRIC if not strong else
+                   "Gaussian-voxel evals/s, fwd+bwd step, 2048^3 vol / 8M "
+                   "Gaussians, z-slab sharded"),
+        "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True,
+        "scaling": "strong" if strong else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded Gaussians + ellipsoid phantom)",
         "config": {"workload": cfg.name, "vol_zyx": list(cfg.vol),
                    "gaussians": cfg.n, "channels": cfg.channels,
@@ -502,7 +568,8 @@ def main():
             "note": ("one MUFU.EX2 per Gaussian-voxel evaluation at 16/clk/SM "
                      "x 148 SMs x max SM clock; E per launch = this rank's "
                      "forward evaluations")}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small:
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small
+            and not strong):
         try:
             out["cpu_baseline"] = cpu_baseline(cfg, inputs)
         except Exception as exc:  # reported, not fatal

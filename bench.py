@@ -187,9 +187,19 @@ class Step:
             self.vox = voxelize.voxelize_gaussians
             self.vox_slab = slab.voxelize_gaussians_slab
             self.vox_l1 = losses.voxelize_gaussians_l1
-        # "fused": L1 inside the voxelization kernels; "dropin": the
-        # reference-compatible voxelize_gaussians + torch L1
-        self.mode = "fused" if impl != "reference" else "dropin"
+        # "graph": the sync-free step (step.FusedL1Step) replayed as a CUDA
+        # graph; "fused": the same kernels through autograd
+        # (losses.voxelize_gaussians_l1); "dropin": the reference-compatible
+        # voxelize_gaussians + torch L1
+        self.mode = "graph" if impl != "reference" else "dropin"
+        self.fstep = None
+        if impl != "reference":
+            from gs_voxelizer_b200.step import FusedL1Step
+            with torch.no_grad():
+                self.params = [h.to(dev) for h in self.host]
+            self.fstep = FusedL1Step(*self.params, cfg.vol, cfg.world,
+                                     cfg.center, self.target,
+                                     denom=self.nvox_global, plan=self.plan)
 
     def forward(self):
         cfg = self.cfg
@@ -222,14 +232,27 @@ class Step:
             t.grad = None
 
     def step(self):
+        if self.mode == "graph":
+            self.fstep.launch()
+            return None
         self.zero_grad()
         loss = self.forward()
         loss.backward()
         return loss
 
+    def check(self):
+        """After a timed graph step (outside the timed region): the pairs
+        fitted the buffer, so the step's results are valid."""
+        if self.mode == "graph" and not self.fstep.finish():
+            raise RuntimeError("pair buffer overflowed during a timed step")
+
     def step_e2e(self):
         """Public-API step with the inputs copied from pinned host memory and
         the loss read back to the host."""
+        if self.mode == "graph":
+            for d, h in zip(self.params, self.host):
+                d.copy_(h, non_blocking=True)
+            return self.fstep.run()
         with torch.no_grad():
             for d, h in zip(self.leaves, self.host):
                 d.copy_(h, non_blocking=True)
@@ -251,8 +274,9 @@ class Step:
 
 # ------------------------------------------------------------------ timing
 
-def time_steps(fn, steps, flush):
-    """Per-step CUDA-event timing with an L2 flush between steps (untimed)."""
+def time_steps(fn, steps, flush, after=None):
+    """Per-step CUDA-event timing with an L2 flush between steps (untimed);
+    `after` runs after each step's stop event (untimed)."""
     total = 0.0
     per = []
     for _ in range(steps):
@@ -262,6 +286,8 @@ def time_steps(fn, steps, flush):
         fn()
         e.record()
         e.synchronize()
+        if after is not None:
+            after()
         ms = s.elapsed_time(e)
         per.append(ms)
         total += ms
@@ -378,24 +404,27 @@ def run_sweep(args):
         inputs = make_inputs(cfg, 1)
         row = {"sweep": args.sweep, "workload": cfg.name, "vol_zyx": list(cfg.vol),
                "gaussians": cfg.n, "channels": cfg.channels}
-        arms = [("fused", "ours"), ("dropin", "ours")]
+        arms = [("graph", "ours"), ("fused", "ours"), ("dropin", "ours")]
         if ref_api.available():
             arms.append(("reference", "reference"))
         for arm, impl in arms:
             st = Step(impl, cfg, 1, 0, inputs)
-            st.mode = "fused" if arm == "fused" else "dropin"
-            if arm == "fused":
+            st.mode = arm if impl == "ours" else "dropin"
+            if arm == "graph":
                 E, n_isect = st.evaluations()
                 row["evals_per_pass"] = E
                 row["intersections"] = n_isect
             for _ in range(max(3, args.warmup)):
                 st.step()
+                st.check()
             torch.cuda.synchronize()
-            fwd, bwd = time_fwd_bwd(st, steps, flush)
-            total, per = time_steps(st.step, steps, flush)
+            total, per = time_steps(st.step, steps, flush, after=st.check)
             step_ms = statistics.median(per)
-            row[arm] = {"fwd_ms": fwd, "bwd_ms": bwd, "step_ms": step_ms,
+            row[arm] = {"step_ms": step_ms,
                         "evals_per_s": 2 * row["evals_per_pass"] / (step_ms / 1e3)}
+            if arm != "graph":
+                fwd, bwd = time_fwd_bwd(st, steps, flush)
+                row[arm].update(fwd_ms=fwd, bwd_ms=bwd)
             del st
             torch.cuda.empty_cache()
         emit(json.dumps(row))
@@ -490,9 +519,13 @@ def main():
     sampler.start()
     launches0 = lib.gsv_launch_count()
     barrier(world)
-    total_ms, per = time_steps(st.step, args.steps, flush)
+    total_ms, per = time_steps(st.step, args.steps, flush, after=st.check)
     barrier(world)
     launches = lib.gsv_launch_count() - launches0
+    if st.fstep is not None:
+        # graph replays launch the captured kernels without passing through
+        # the library's host launch counter
+        launches += st.fstep.launches_per_step * args.steps
     clocks = sampler.stop()
     total_ms = max_over_ranks(total_ms, world)
     ms_per_step = total_ms / args.steps
@@ -505,6 +538,18 @@ def main():
     e2e_ms, _ = time_steps(st.step_e2e, args.steps, flush)
     e2e_ms = max_over_ranks(e2e_ms, world) / args.steps
 
+    autograd = None
+    if impl != "reference":
+        # the same fused kernels through autograd (one host read of the pair
+        # count per step, ~25 launches from Python)
+        st.mode = "fused"
+        for _ in range(3):
+            st.step()
+        a_ms, _ = time_steps(st.step, args.steps, flush)
+        a_ms = max_over_ranks(a_ms, world) / args.steps
+        autograd = {"ms_per_step": a_ms, "value": evals_per_step / (a_ms / 1e3),
+                    "api": "optim_to_render + losses.voxelize_gaussians_l1 "
+                           "+ loss.backward()"}
     fwd_ms, bwd_ms = time_fwd_bwd(st, max(3, args.steps // 2), flush)
     fwd_ms, bwd_ms = max_over_ranks(fwd_ms, world), max_over_ranks(bwd_ms, world)
 
@@ -519,7 +564,8 @@ def main():
         d_ms = max_over_ranks(d_ms, world) / args.steps
         dropin = {"ms_per_step": d_ms, "value": evals_per_step / (d_ms / 1e3),
                   "api": "optim_to_render + voxelize_gaussians + torch l1_loss"}
-        st.mode = "fused"
+    if impl != "reference":
+        st.mode = "fused"  # kernel timing below runs the eager launches
 
     out = {
         "metric": (METRIC if not strong else
@@ -538,11 +584,18 @@ def main():
                    "l2": "flushed between timed steps (256 MB write)",
                    "loss": ("L1 vs phantom, torch l1_loss" if impl == "reference"
                             else "L1 vs phantom, fused into the voxelization "
-                                 "kernels (gs_voxelizer_b200.losses)")},
-        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "dropin": dropin,
+                                 "kernels"),
+                   "step": ("reference API through autograd" if impl == "reference"
+                            else "gs_voxelizer_b200.step.FusedL1Step: sync-free, "
+                                 "replayed as a CUDA graph")},
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "fwd_bwd_split": ("autograd step" if impl == "reference" else
+                          "autograd fused step (losses.voxelize_gaussians_l1)"),
+        "autograd": autograd, "dropin": dropin,
         "e2e": {"value": evals_per_step / (e2e_ms / 1e3), "unit": UNIT,
                 "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": st.in_bytes, "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": st.in_bytes,
+                "d2h_bytes_per_step": 8 if st.fstep is not None else 4},
         "clocks": clocks,
     }
     if impl == "reference":

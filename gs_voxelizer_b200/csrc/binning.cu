@@ -97,7 +97,7 @@ expand_pairs_kernel(int n, const int *__restrict__ tmin,
                     atomicAdd(counter + tile, 1);
                 } else {
                     const int slot = atomicAdd(counter + tile, 1);
-                    if (slot < capacity) {
+                    if (slot >= 0 && slot < capacity) {
                         ids_out[slot] = (int)(w * 32 + owner);
                     } else {
                         *error_flag = 1;
@@ -188,11 +188,15 @@ scan_partials_top_kernel(long long *__restrict__ partials, int nblocks) {
     if (threadIdx.x == 0) partials[nblocks] = total;
 }
 
-// tile_bins[t] = count ? (offset, offset + count) : (0, 0); cursor[t] = offset
+// tile_bins[t] = count ? (offset, offset + count) : (0, 0); cursor[t] = offset.
+// Offsets and ends are clamped to `cap` (the id buffer's capacity): when the
+// pairs outnumber the buffer, every range still lies inside it, the scatter
+// drops what does not fit, and the caller detects the overflow from the count.
 __global__ void __launch_bounds__(kScanThreads)
 scan_bins_kernel(const int *__restrict__ counts, long long n,
                  const long long *__restrict__ partials,
-                 int2 *__restrict__ tile_bins, int *__restrict__ cursor) {
+                 int2 *__restrict__ tile_bins, int *__restrict__ cursor,
+                 long long cap) {
     __shared__ long long smem[32];
     const long long base = (long long)blockIdx.x * kScanTile;
     // each thread owns kScanItems consecutive tiles
@@ -209,9 +213,10 @@ scan_bins_kernel(const int *__restrict__ counts, long long n,
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k) {
         if (first + k < n) {
-            const int off = (int)run;
+            const int off = (int)min(run, cap);
+            const int end = (int)min(run + v[k], cap);
             tile_bins[first + k] =
-                v[k] > 0 ? make_int2(off, off + v[k]) : make_int2(0, 0);
+                v[k] > 0 ? make_int2(off, end) : make_int2(0, 0);
             cursor[first + k] = off;
             run += v[k];
         }
@@ -440,14 +445,15 @@ size_t bin_workspace_bytes(long long ntiles, long long nisect) {
 // overwritten with the cursors). Exposed for the backward planner too.
 cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *partials, int *tile_bins,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, long long cap) {
     const long long nblocks = (ntiles + kScanTile - 1) / kScanTile;
     if (nblocks > 1024LL * 64) return cudaErrorInvalidValue;
     scan_partials_kernel<int><<<(unsigned)nblocks, kScanThreads, 0, stream>>>(
         counts, ntiles, partials);
     scan_partials_top_kernel<<<1, 1024, 0, stream>>>(partials, (int)nblocks);
     scan_bins_kernel<<<(unsigned)nblocks, kScanThreads, 0, stream>>>(
-        counts, ntiles, partials, reinterpret_cast<int2 *>(tile_bins), counts);
+        counts, ntiles, partials, reinterpret_cast<int2 *>(tile_bins), counts,
+        cap);
     count_launches(3);
     return cudaGetLastError();
 }
@@ -477,7 +483,8 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
             n, tmin, tmax, Tx, Ty, tz0, tz1, counts, nullptr, 0, flags + 1);
         count_launches(1);
     }
-    if ((err = scan_counts_to_bins(counts, ntiles, partials, tile_bins, stream)))
+    if ((err = scan_counts_to_bins(counts, ntiles, partials, tile_bins, stream,
+                                   nisect)))
         return err;
     if (n <= 0 || nisect <= 0) return cudaGetLastError();
     {

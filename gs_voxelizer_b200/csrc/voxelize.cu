@@ -30,7 +30,7 @@ namespace gsv {
 
 cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *partials, int *tile_bins,
-                                cudaStream_t stream);
+                                cudaStream_t stream, long long cap);
 size_t l1_workspace_bytes(long long n);
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
@@ -1017,7 +1017,7 @@ static cudaError_t launch_bwd_plan(const int2 *bins, long long ntiles,
     const unsigned tblocks = (unsigned)((ntiles + 255) / 256);
     item_count_kernel<<<tblocks, 256, 0, stream>>>(bins, ntiles, item_counts);
     cudaError_t err = scan_counts_to_bins(item_counts, ntiles, partials,
-                                          item_bins, stream);
+                                          item_bins, stream, LLONG_MAX);
     if (err) return err;
     item_fill_kernel<<<tblocks, 256, 0, stream>>>(
         reinterpret_cast<const int2 *>(item_bins), ntiles, item_tile);

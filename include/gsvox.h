@@ -263,7 +263,13 @@ GSV_API int gsv_l1_loss_backward(int64_t n, const float *vol,
  *    dL/dvol = sign(out_vol - target) * grad_loss[0] / denom while staging
  *    each tile (no gradient volume is read or written) and writes the
  *    per-Gaussian gradients like gsv_voxelize_backward_per_gaussian.
- * num_intersects: the slab's pair count (gsv_count_slab_intersects).
+ * num_intersects: the slab's pair count (gsv_count_slab_intersects), or any
+ * upper bound of it (a capacity), so that a step needs no host read of the
+ * count: ids past the true count stay unused. If the true count exceeds
+ * num_intersects, the tile ranges are clamped to it (no access outside the
+ * buffers) and the results are invalid; the caller compares the count that
+ * gsv_count_slab_intersects left in device memory and re-runs with a larger
+ * capacity. Both calls of a step take the same num_intersects.
  * No reference counterpart (fuses bindings.cu:261, :362 and :589 with the
  * loss the reference's callers compute in PyTorch).
  */

@@ -388,23 +388,25 @@ struct BwdSmem {
     static constexpr int kWarp = 8 * kRow;          // floats per warp buffer
 };
 
-// Stages dL/dvol of one tile. LOSS: dL/dvol is not materialised; it is the
-// fused L1 gradient sign(vol - target) * scale, computed from the volume
-// (passed as `grad`) and the target here.
+// Stages dL/dvol of one tile, multiplied by 2^K with K chosen from the
+// tile's largest |dL/dvol| so that the largest staged value lies in
+// [2^64, 2^65) (K <= 126); returns K, or INT_MIN when the tile's gradient is
+// zero (the tile contributes nothing). LOSS: dL/dvol is not materialised; it
+// is the fused L1 gradient sign(vol - target) * scale, computed from the
+// volume (passed as `grad`) and the target here.
 template <int C, bool LOSS>
-__device__ __forceinline__ void stage_grad_tile(const Geom &g,
+__device__ __forceinline__ int stage_grad_tile(const Geom &g,
                                                 const float *__restrict__ grad,
                                                 const float *__restrict__ target,
                                                 float scale, int ox, int oy,
                                                 int oz, float *buf, int lane) {
     using S = BwdSmem<C>;
     // 64 (z, y) rows of 8*C floats; lane handles rows lane and lane + 32
+    float v[2][8 * C];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int row = lane + 32 * h;
-        const int zl = row >> 3, yl = row & 7;
-        const int z = oz + zl, y = oy + yl;
-        float v[8 * C];
+        const int z = oz + (row >> 3), y = oy + (row & 7);
         const bool row_in = (z < g.z_end()) && (y < g.Y);
         const int nx = row_in ? min(kTile, g.X - ox) : 0;
         const size_t base =
@@ -416,37 +418,62 @@ __device__ __forceinline__ void stage_grad_tile(const Geom &g,
             for (int q = 0; q < 2 * C; ++q) {
                 const float4 t =
                     __ldg(reinterpret_cast<const float4 *>(grad + base) + q);
-                v[4 * q + 0] = t.x;
-                v[4 * q + 1] = t.y;
-                v[4 * q + 2] = t.z;
-                v[4 * q + 3] = t.w;
+                v[h][4 * q + 0] = t.x;
+                v[h][4 * q + 1] = t.y;
+                v[h][4 * q + 2] = t.z;
+                v[h][4 * q + 3] = t.w;
                 if (LOSS) {
                     const float4 u =
                         __ldg(reinterpret_cast<const float4 *>(target + base) + q);
-                    v[4 * q + 0] -= u.x;
-                    v[4 * q + 1] -= u.y;
-                    v[4 * q + 2] -= u.z;
-                    v[4 * q + 3] -= u.w;
+                    v[h][4 * q + 0] -= u.x;
+                    v[h][4 * q + 1] -= u.y;
+                    v[h][4 * q + 2] -= u.z;
+                    v[h][4 * q + 3] -= u.w;
                 }
             }
         } else {
 #pragma unroll
             for (int q = 0; q < 8 * C; ++q) {
-                v[q] = (q < nx * C) ? __ldg(grad + base + q) : 0.f;
-                if (LOSS) v[q] -= (q < nx * C) ? __ldg(target + base + q) : 0.f;
+                v[h][q] = (q < nx * C) ? __ldg(grad + base + q) : 0.f;
+                if (LOSS) v[h][q] -= (q < nx * C) ? __ldg(target + base + q) : 0.f;
             }
         }
         if (LOSS) {
 #pragma unroll
             for (int q = 0; q < 8 * C; ++q)
-                v[q] = v[q] > 0.f ? scale : (v[q] < 0.f ? -scale : 0.f);
+                v[h][q] = v[h][q] > 0.f ? scale : (v[h][q] < 0.f ? -scale : 0.f);
         }
+    }
+    float m = 0.f;
+    bool nan = false;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int q = 0; q < 8 * C; ++q) {
+            m = fmaxf(m, fabsf(v[h][q]));
+            nan |= v[h][q] != v[h][q];
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // NaNs propagate as in the reference (staged unscaled in magnitude terms)
+    if (__any_sync(0xffffffffu, nan)) m = fmaxf(m, 1.f);
+    if (!(m > 0.f)) return INT_MIN;
+    const int e = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;
+    const int K = min(126, 64 - e);
+    const float gk = __uint_as_float((unsigned)(127 + K) << 23);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = lane + 32 * h;
+        const int zl = row >> 3, yl = row & 7;
 #pragma unroll
         for (int x = 0; x < 8; ++x)
 #pragma unroll
             for (int c = 0; c < C; ++c)
-                buf[yl * S::kRow + x * S::kCol + zl * C + c] = v[x * C + c];
+                buf[yl * S::kRow + x * S::kCol + zl * C + c] =
+                    v[h][x * C + c] * gk;
     }
+    return K;
 }
 
 // Sums over one y-row of the tile for one Gaussian (per lane).
@@ -454,12 +481,18 @@ struct RowSums {
     float R0, R1, R2, Rx0, Rxx, Rx1;
 };
 
+__device__ __forceinline__ float pick(const float2 (&p)[4], int j) {
+    return (j & 1) ? p[j >> 1].y : p[j >> 1].x;
+}
+
+// Exact path: alpha = 2^s, counted where s >= thr (and s <= 0 unless the
+// Gaussian is robustly positive definite), as the reference culls.
 template <int C, bool CHECK_SIGN>
 __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
                                            float thr, float A, float Cz,
                                            float E, float Dy, float By2,
-                                           float Fy, const float (&dz)[8],
-                                           const float (&dz2)[8],
+                                           float Fy, const float2 (&dzp)[4],
+                                           const float2 (&dsp)[4],
                                            const float (&I)[C],
                                            float (&W)[C]) {
     using S = BwdSmem<C>;
@@ -482,7 +515,8 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
         float T0 = 0.f, T1 = 0.f, T2 = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float s = fmaf(dz[j], fmaf(Cz, dz[j], L), P);
+            const float dzj = pick(dzp, j), dsj = pick(dsp, j);
+            const float s = fmaf(dzj, fmaf(Cz, dzj, L), P);
             if (C == 1) {
                 // w = alpha * dL/dvol; the three moment updates are
                 // predicated on the cull test (no select instruction)
@@ -495,7 +529,7 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
                         "@p fma.rn.f32 %1, %5, %6, %1;\n\t"
                         "@p fma.rn.f32 %2, %5, %7, %2;\n\t}"
                         : "+f"(T0), "+f"(T1), "+f"(T2)
-                        : "f"(s), "f"(thr), "f"(w), "f"(dz[j]), "f"(dz2[j]));
+                        : "f"(s), "f"(thr), "f"(w), "f"(dzj), "f"(dsj));
                 } else {
                     asm("{\n\t.reg .pred p;\n\t"
                         "setp.ge.f32 p, %3, %4;\n\t"
@@ -503,7 +537,7 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
                         "@p fma.rn.f32 %1, %5, %6, %1;\n\t"
                         "@p fma.rn.f32 %2, %5, %7, %2;\n\t}"
                         : "+f"(T0), "+f"(T1), "+f"(T2)
-                        : "f"(s), "f"(thr), "f"(w), "f"(dz[j]), "f"(dz2[j]));
+                        : "f"(s), "f"(thr), "f"(w), "f"(dzj), "f"(dsj));
                 }
                 continue;
             }
@@ -521,8 +555,8 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
                 w = a * h;
             }
             T0 += w;
-            T1 = fmaf(w, dz[j], T1);
-            T2 = fmaf(w, dz2[j], T2);
+            T1 = fmaf(w, dzj, T1);
+            T2 = fmaf(w, dsj, T2);
         }
         r.R0 += T0;
         r.R1 += T1;
@@ -535,15 +569,289 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
     return r;
 }
 
+// Flush path (robustly positive-definite Gaussians): the row constant By2s
+// carries -(thr + 126), so alpha' = 2^(s - thr - 126) is below the smallest
+// normal float exactly when s < thr and ex2.approx.ftz returns 0 there: the
+// cull costs no instruction. alpha = alpha' * 2^(thr + 126) is restored on
+// the lane's sums. C = 1: two z-voxels per paired FP32 instruction
+// (FFMA2 / FMUL2 / FADD2), sums kept as pairs until the end of the row.
+__device__ __forceinline__ RowSums bwd_row_flush1(const float *colbase,
+                                                  float mx, float A, float Cz,
+                                                  float E, float Dy,
+                                                  float By2s, float Fy,
+                                                  const float2 (&dzp)[4],
+                                                  const float2 (&dsp)[4]) {
+    using S = BwdSmem<1>;
+    const float2 z2 = f2(0.f), Cz2 = f2(Cz);
+    float2 R0 = z2, R1 = z2, R2 = z2, Rx0 = z2, Rxx = z2, Rx1 = z2;
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+        const float dx = mx - ((float)x + 0.5f);
+        const float2 dx2 = f2(dx);
+        const float2 P = f2(fmaf(dx, fmaf(A, dx, Dy), By2s));
+        const float2 L = f2(fmaf(E, dx, Fy));
+        const float4 ga = reinterpret_cast<const float4 *>(colbase + x * S::kCol)[0];
+        const float4 gb = reinterpret_cast<const float4 *>(colbase + x * S::kCol)[1];
+        const float2 g[4] = {make_float2(ga.x, ga.y), make_float2(ga.z, ga.w),
+                             make_float2(gb.x, gb.y), make_float2(gb.z, gb.w)};
+        float2 T0, T1, T2;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 sp = __ffma2_rn(dzp[k], __ffma2_rn(Cz2, dzp[k], L), P);
+            const float2 w = __fmul2_rn(make_float2(ex2(sp.x), ex2(sp.y)), g[k]);
+            if (k == 0) {
+                T0 = w;
+                T1 = __fmul2_rn(w, dzp[0]);
+                T2 = __fmul2_rn(w, dsp[0]);
+            } else {
+                T0 = __fadd2_rn(T0, w);
+                T1 = __ffma2_rn(w, dzp[k], T1);
+                T2 = __ffma2_rn(w, dsp[k], T2);
+            }
+        }
+        R0 = __fadd2_rn(R0, T0);
+        R1 = __fadd2_rn(R1, T1);
+        R2 = __fadd2_rn(R2, T2);
+        const float2 u = __fmul2_rn(dx2, T0);
+        Rx0 = __fadd2_rn(Rx0, u);
+        Rxx = __ffma2_rn(u, dx2, Rxx);
+        Rx1 = __ffma2_rn(dx2, T1, Rx1);
+    }
+    RowSums r;
+    r.R0 = R0.x + R0.y;
+    r.R1 = R1.x + R1.y;
+    r.R2 = R2.x + R2.y;
+    r.Rx0 = Rx0.x + Rx0.y;
+    r.Rxx = Rxx.x + Rxx.y;
+    r.Rx1 = Rx1.x + Rx1.y;
+    return r;
+}
+
+// Flush path for C > 1 (scalar): as bwd_row without the cull test.
+template <int C>
+__device__ __forceinline__ RowSums bwd_row_flush(const float *colbase,
+                                                 float mx, float A, float Cz,
+                                                 float E, float Dy, float By2s,
+                                                 float Fy,
+                                                 const float2 (&dzp)[4],
+                                                 const float2 (&dsp)[4],
+                                                 const float (&I)[C],
+                                                 float (&W)[C]) {
+    using S = BwdSmem<C>;
+    RowSums r = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+        const float dx = mx - ((float)x + 0.5f);
+        const float P = fmaf(dx, fmaf(A, dx, Dy), By2s);
+        const float L = fmaf(E, dx, Fy);
+        float gv[8 * C];
+#pragma unroll
+        for (int q4 = 0; q4 < 2 * C; ++q4) {
+            const float4 t =
+                reinterpret_cast<const float4 *>(colbase + x * S::kCol)[q4];
+            gv[4 * q4 + 0] = t.x;
+            gv[4 * q4 + 1] = t.y;
+            gv[4 * q4 + 2] = t.z;
+            gv[4 * q4 + 3] = t.w;
+        }
+        float T0 = 0.f, T1 = 0.f, T2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float dzj = pick(dzp, j), dsj = pick(dsp, j);
+            const float a = ex2(fmaf(dzj, fmaf(Cz, dzj, L), P));
+            float h = I[0] * gv[j * C];
+#pragma unroll
+            for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[j * C + c], h);
+#pragma unroll
+            for (int c = 0; c < C; ++c) W[c] = fmaf(a, gv[j * C + c], W[c]);
+            const float w = a * h;
+            T0 += w;
+            T1 = fmaf(w, dzj, T1);
+            T2 = fmaf(w, dsj, T2);
+        }
+        r.R0 += T0;
+        r.R1 += T1;
+        r.R2 += T2;
+        const float u = dx * T0;
+        r.Rx0 += u;
+        r.Rxx = fmaf(u, dx, r.Rxx);
+        r.Rx1 = fmaf(dx, T1, r.Rx1);
+    }
+    return r;
+}
+
+// Lanes of a work item of m Gaussians: r row groups of gs = 32 / r lanes
+// (r the largest power of two <= 8 with m * r <= 32); lane = sub * gs + gi
+// evaluates Gaussian slot gi over the tile's y-rows [sub * rows, +rows).
+struct ItemLanes {
+    int gs, gi, sub, rows;
+    bool valid;
+};
+
+__device__ __forceinline__ ItemLanes item_lanes(int m, int lane) {
+    int r = 1;
+    while (r < 8 && m * r * 2 <= 32) r <<= 1;
+    ItemLanes L;
+    L.gs = 32 / r;
+    L.gi = lane & (L.gs - 1);
+    L.sub = lane >> (__ffs(L.gs) - 1);
+    L.rows = 8 / r;
+    L.valid = L.gi < m;
+    return L;
+}
+
+// One work item's evaluation, from the staged (2^K-scaled) dL/dvol tile in
+// `buf` and the lane's record (r0 tile-relative; invalid lanes: thr NaN),
+// to the per-Gaussian atomics.
+template <int C>
+__device__ __forceinline__ void bwd_item(const float *buf, int K,
+                                         const ItemLanes &L, int gid,
+                                         const float4 &r0, const float4 &r1,
+                                         const float4 &r2, const float4 &r3,
+                                         const float2 *__restrict__ conics,
+                                         float *__restrict__ pos_grad,
+                                         float *__restrict__ conic_grad,
+                                         float *__restrict__ int_grad) {
+    using S = BwdSmem<C>;
+    float I[C];
+    record_intensity<C>(r2, r3, I);
+    const float thr = r0.w;
+    const bool all_robust = __all_sync(0xffffffffu, robust_flag(thr));
+    // flush path: every valid lane robust with thr >= -126, and the tile's
+    // scale leaves 2^(thr + 126 - K) finite (K >= -1)
+    const bool flush =
+        K >= -1 && __all_sync(0xffffffffu,
+                              !L.valid || (robust_flag(thr) && thr >= -126.f));
+    const float shift = L.valid ? thr + 126.f : __int_as_float(0x7f800000);
+    float2 dzp[4], dsp[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        dzp[k] = make_float2(r0.z - ((float)(2 * k) + 0.5f),
+                             r0.z - ((float)(2 * k + 1) + 0.5f));
+        dsp[k] = __fmul2_rn(dzp[k], dzp[k]);
+    }
+
+    // sums over the Gaussian's voxels of w-weighted monomials of d, where
+    // w = alpha * h and h = sum_c I_c dL/dvol_c (C > 1) or dL/dvol (C = 1)
+    float Sxx = 0.f, Syy = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f, Syz = 0.f;
+    float Vx = 0.f, Vy = 0.f, Vz = 0.f;
+    float W[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) W[c] = 0.f;
+
+#pragma unroll 1
+    for (int q = 0; q < L.rows; ++q) {
+        const int yl = L.sub * L.rows + q;
+        const float dy = r0.y - ((float)yl + 0.5f);
+        const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
+        const float *colbase = buf + yl * S::kRow;
+        RowSums rs;
+        if (flush) {
+            if (C == 1)
+                rs = bwd_row_flush1(colbase, r0.x, r1.x, r1.z, r2.x, Dy,
+                                    By2 - shift, Fy, dzp, dsp);
+            else
+                rs = bwd_row_flush<C>(colbase, r0.x, r1.x, r1.z, r2.x, Dy,
+                                      By2 - shift, Fy, dzp, dsp, I, W);
+        } else if (all_robust) {
+            rs = bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x, Dy,
+                                   By2, Fy, dzp, dsp, I, W);
+        } else {
+            rs = bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z, r2.x, Dy,
+                                  By2, Fy, dzp, dsp, I, W);
+        }
+        if (C == 1) W[0] += rs.R0;  // intensity grad = sum(w) (C = 1)
+        Sxx += rs.Rxx;
+        Szz += rs.R2;
+        Sxz += rs.Rx1;
+        Vx += rs.Rx0;
+        Vz += rs.R1;
+        Syy = fmaf(dy * dy, rs.R0, Syy);
+        Sxy = fmaf(dy, rs.Rx0, Sxy);
+        Syz = fmaf(dy, rs.R1, Syz);
+        Vy = fmaf(dy, rs.R0, Vy);
+    }
+
+    // combine row groups (lanes gi, gi+gs, gi+2gs, ...)
+    for (int o = L.gs; o < 32; o <<= 1) {
+        Sxx += __shfl_xor_sync(0xffffffffu, Sxx, o);
+        Syy += __shfl_xor_sync(0xffffffffu, Syy, o);
+        Szz += __shfl_xor_sync(0xffffffffu, Szz, o);
+        Sxy += __shfl_xor_sync(0xffffffffu, Sxy, o);
+        Sxz += __shfl_xor_sync(0xffffffffu, Sxz, o);
+        Syz += __shfl_xor_sync(0xffffffffu, Syz, o);
+        Vx += __shfl_xor_sync(0xffffffffu, Vx, o);
+        Vy += __shfl_xor_sync(0xffffffffu, Vy, o);
+        Vz += __shfl_xor_sync(0xffffffffu, Vz, o);
+#pragma unroll
+        for (int c = 0; c < C; ++c) W[c] += __shfl_xor_sync(0xffffffffu, W[c], o);
+    }
+
+    if (L.valid && L.sub == 0) {
+        // undo the staging scale 2^K and, on the flush path, the exponent
+        // shift 2^-(thr + 126)
+        const float corr = flush ? ex2(fminf(shift - (float)K, 127.f))
+                                 : __uint_as_float((unsigned)(127 - K) << 23);
+#pragma unroll
+        for (int c = 0; c < C; ++c) W[c] *= corr;
+        const float k = ((C == 1) ? I[0] : 1.f) * corr;  // sigma_grad = I * w
+        const float2 ab = conics[3 * gid + 0], cd = conics[3 * gid + 1],
+                     ef = conics[3 * gid + 2];
+        const float a_ = ab.x, b_ = ab.y, c_ = cd.x, d_ = cd.y, e_ = ef.x,
+                    f_ = ef.y;
+        const float vx = k * Vx, vy = k * Vy, vz = k * Vz;
+        red_add4(pos_grad + 4 * (size_t)gid, -(a_ * vx + b_ * vy + c_ * vz),
+                 -(b_ * vx + d_ * vy + e_ * vz), -(c_ * vx + e_ * vy + f_ * vz),
+                 0.f);
+        float *cg = conic_grad + 6 * (size_t)gid;
+        red_add2(cg + 0, -0.5f * k * Sxx, -k * Sxy);
+        red_add2(cg + 2, -k * Sxz, -0.5f * k * Syy);
+        red_add2(cg + 4, -k * Syz, -0.5f * k * Szz);
+        float *ig = int_grad + (size_t)C * gid;
+        if (C == 4) {
+            red_add4(ig, W[0], W[C > 1 ? 1 : 0], W[C > 2 ? 2 : 0],
+                     W[C > 3 ? 3 : 0]);
+        } else if (C == 2) {
+            red_add2(ig, W[0], W[C > 1 ? 1 : 0]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < C; ++c) red_add(ig + c, W[c]);
+        }
+    }
+}
+
+// Record of an item's lane: loaded, made tile-relative; invalid lanes get
+// thr = NaN (nothing passes) and zero coefficients.
+template <int R>
+__device__ __forceinline__ void item_record(const float4 *__restrict__ rec,
+                                            int gid, bool valid, int ox,
+                                            int oy, int oz, float4 &r0,
+                                            float4 &r1, float4 &r2,
+                                            float4 &r3) {
+    r0 = make_float4(0.f, 0.f, 0.f, __int_as_float(0x7f800001));
+    r1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    r2 = r1;
+    r3 = r1;
+    if (valid) {
+        r0 = rec[(size_t)gid * R + 0];
+        r1 = rec[(size_t)gid * R + 1];
+        r2 = rec[(size_t)gid * R + 2];
+        if (R == 4) r3 = rec[(size_t)gid * R + 3];
+        r0.x -= (float)ox;
+        r0.y -= (float)oy;
+        r0.z -= (float)oz;
+    }
+}
+
+// Per-Gaussian backward: persistent warps take items from an atomic
+// counter; each item stages its tile, loads its records and evaluates.
 template <int C, bool LOSS>
-__global__ void __launch_bounds__(kBwdWarps * 32, C <= 2 ? 6 : 4)
-vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
-                     const int *__restrict__ ids,
+__global__ void __launch_bounds__(kBwdWarps * 32, C == 1 ? 5 : (C == 2 ? 6 : 4))
+vox_bwd_gauss_kernel(Geom g, const int *__restrict__ ids,
                      const float4 *__restrict__ rec,
                      const float2 *__restrict__ conics,
                      const float *__restrict__ grad,
-                     const int2 *__restrict__ item_bins,
-                     const int *__restrict__ item_tile,
+                     const int4 *__restrict__ item_desc,
                      const long long *__restrict__ item_total,
                      int *__restrict__ work_counter,
                      float *__restrict__ pos_grad,
@@ -564,125 +872,20 @@ vox_bwd_gauss_kernel(Geom g, const int2 *__restrict__ bins,
         if (lane == 0) item = atomicAdd(work_counter, 1);
         item = __shfl_sync(0xffffffffu, item, 0);
         if (item >= total) break;
-
-        const int tile = item_tile[item];
-        const int2 range = bins[tile];
-        const int bucket = item - item_bins[tile].x;
-        const int start = range.x + 32 * bucket;
-        const int m = min(32, range.y - start);
-        int r = 1;
-        while (r < 8 && m * r * 2 <= 32) r <<= 1;
-        const int gs = 32 / r;           // lanes per row group
-        const int gi = lane % gs;        // Gaussian slot
-        const int sub = lane / gs;       // row group
-        const int rows = 8 / r;
-        const bool valid = gi < m;
-
+        const int4 d = __ldg(item_desc + item);
+        const ItemLanes L = item_lanes(d.z, lane);
         int ox, oy, oz;
-        tile_coords(g, tile, ox, oy, oz);
+        tile_coords(g, d.x, ox, oy, oz);
         __syncwarp();
-        stage_grad_tile<C, LOSS>(g, grad, target, scale, ox, oy, oz, buf, lane);
+        const int K = stage_grad_tile<C, LOSS>(g, grad, target, scale, ox, oy,
+                                               oz, buf, lane);
         __syncwarp();
-
-        int gid = 0;
-        // invalid lanes get thr = +inf with the robust bit: nothing passes
-        float4 r0 = make_float4(0.f, 0.f, 0.f, __int_as_float(0x7f800001));
-        float4 r1 = make_float4(0.f, 0.f, 0.f, 0.f), r2 = r1, r3 = r1;
-        if (valid) {
-            gid = ids[start + gi];
-            r0 = rec[(size_t)gid * R + 0];
-            r1 = rec[(size_t)gid * R + 1];
-            r2 = rec[(size_t)gid * R + 2];
-            if (R == 4) r3 = rec[(size_t)gid * R + 3];
-            r0.x -= (float)ox;
-            r0.y -= (float)oy;
-            r0.z -= (float)oz;
-        }
-        float I[C];
-        record_intensity<C>(r2, r3, I);
-        const float thr = r0.w;
-        const bool all_robust = __all_sync(0xffffffffu, robust_flag(thr));
-        float dz[8], dz2[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            dz[j] = r0.z - ((float)j + 0.5f);
-            dz2[j] = dz[j] * dz[j];
-        }
-
-        // sums over the Gaussian's voxels of w-weighted monomials of d, where
-        // w = alpha * h and h = sum_c I_c dL/dvol_c (C > 1) or dL/dvol (C = 1)
-        float Sxx = 0.f, Syy = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f, Syz = 0.f;
-        float Vx = 0.f, Vy = 0.f, Vz = 0.f;
-        float W[C];
-#pragma unroll
-        for (int c = 0; c < C; ++c) W[c] = 0.f;
-
-#pragma unroll 1
-        for (int q = 0; q < rows; ++q) {
-            const int yl = sub * rows + q;
-            const float dy = r0.y - ((float)yl + 0.5f);
-            const float By2 = r1.y * dy * dy, Dy = r1.w * dy, Fy = r2.y * dy;
-            const float *colbase = buf + yl * S::kRow;
-            const RowSums rs =
-                all_robust
-                    ? bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
-                                        Dy, By2, Fy, dz, dz2, I, W)
-                    : bwd_row<C, true>(colbase, r0.x, thr, r1.x, r1.z, r2.x,
-                                       Dy, By2, Fy, dz, dz2, I, W);
-            if (C == 1) W[0] += rs.R0;  // intensity grad = sum(w) (C = 1)
-            Sxx += rs.Rxx;
-            Szz += rs.R2;
-            Sxz += rs.Rx1;
-            Vx += rs.Rx0;
-            Vz += rs.R1;
-            Syy = fmaf(dy * dy, rs.R0, Syy);
-            Sxy = fmaf(dy, rs.Rx0, Sxy);
-            Syz = fmaf(dy, rs.R1, Syz);
-            Vy = fmaf(dy, rs.R0, Vy);
-        }
-
-        // combine row groups (lanes gi, gi+gs, gi+2gs, ...)
-        for (int o = gs; o < 32; o <<= 1) {
-            Sxx += __shfl_xor_sync(0xffffffffu, Sxx, o);
-            Syy += __shfl_xor_sync(0xffffffffu, Syy, o);
-            Szz += __shfl_xor_sync(0xffffffffu, Szz, o);
-            Sxy += __shfl_xor_sync(0xffffffffu, Sxy, o);
-            Sxz += __shfl_xor_sync(0xffffffffu, Sxz, o);
-            Syz += __shfl_xor_sync(0xffffffffu, Syz, o);
-            Vx += __shfl_xor_sync(0xffffffffu, Vx, o);
-            Vy += __shfl_xor_sync(0xffffffffu, Vy, o);
-            Vz += __shfl_xor_sync(0xffffffffu, Vz, o);
-#pragma unroll
-            for (int c = 0; c < C; ++c)
-                W[c] += __shfl_xor_sync(0xffffffffu, W[c], o);
-        }
-
-        if (valid && sub == 0) {
-            const float k = (C == 1) ? I[0] : 1.f;  // sigma_grad = I * w (C=1)
-            const float2 ab = conics[3 * gid + 0], cd = conics[3 * gid + 1],
-                         ef = conics[3 * gid + 2];
-            const float a_ = ab.x, b_ = ab.y, c_ = cd.x, d_ = cd.y, e_ = ef.x,
-                        f_ = ef.y;
-            const float vx = k * Vx, vy = k * Vy, vz = k * Vz;
-            red_add4(pos_grad + 4 * (size_t)gid,
-                     -(a_ * vx + b_ * vy + c_ * vz),
-                     -(b_ * vx + d_ * vy + e_ * vz),
-                     -(c_ * vx + e_ * vy + f_ * vz), 0.f);
-            float *cg = conic_grad + 6 * (size_t)gid;
-            red_add2(cg + 0, -0.5f * k * Sxx, -k * Sxy);
-            red_add2(cg + 2, -k * Sxz, -0.5f * k * Syy);
-            red_add2(cg + 4, -k * Syz, -0.5f * k * Szz);
-            float *ig = int_grad + (size_t)C * gid;
-            if (C == 4) {
-                red_add4(ig, W[0], W[C > 1 ? 1 : 0], W[C > 2 ? 2 : 0],
-                         W[C > 3 ? 3 : 0]);
-            } else if (C == 2) {
-                red_add2(ig, W[0], W[C > 1 ? 1 : 0]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < C; ++c) red_add(ig + c, W[c]);
-            }
-        }
+        if (K == INT_MIN) continue;  // dL/dvol is zero on this tile
+        const int gid = L.valid ? ids[d.y + L.gi] : 0;
+        float4 r0, r1, r2, r3;
+        item_record<R>(rec, gid, L.valid, ox, oy, oz, r0, r1, r2, r3);
+        bwd_item<C>(buf, K, L, gid, r0, r1, r2, r3, conics, pos_grad,
+                    conic_grad, int_grad);
     }
 }
 
@@ -697,13 +900,19 @@ item_count_kernel(const int2 *__restrict__ bins, long long ntiles,
     counts[t] = (n + 31) / 32;
 }
 
+// Item descriptors (tile, first pair, number of Gaussians <= 32, 0).
 __global__ void __launch_bounds__(256)
-item_fill_kernel(const int2 *__restrict__ item_bins, long long ntiles,
-                 int *__restrict__ item_tile) {
+item_fill_kernel(const int2 *__restrict__ bins,
+                 const int2 *__restrict__ item_bins, long long ntiles,
+                 int4 *__restrict__ item_desc) {
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= ntiles) return;
     const int2 r = item_bins[t];
-    for (int k = r.x; k < r.y; ++k) item_tile[k] = (int)t;
+    const int2 range = bins[t];
+    for (int k = r.x; k < r.y; ++k) {
+        const int start = range.x + 32 * (k - r.x);
+        item_desc[k] = make_int4((int)t, start, min(32, range.y - start), 0);
+    }
 }
 
 // ------------------------------------------------------ backward (per voxel)
@@ -865,7 +1074,7 @@ zero_grads_kernel(int n, int C, float *__restrict__ pos_grad,
 // ------------------------------------------------------------ host launchers
 
 struct VoxLayout {
-    size_t rec, item_counts, item_bins, partials, item_tile, counter,
+    size_t rec, item_counts, item_bins, partials, item_desc, counter,
         tile_loss, loss_partials, total;
 };
 
@@ -886,8 +1095,8 @@ VoxLayout vox_layout(long long n, int channels, long long ntiles,
     off = align256v(off + sizeof(int2) * (size_t)ntiles);
     L.partials = off;
     off = align256v(off + sizeof(long long) * (size_t)(nblocks + 1));
-    L.item_tile = off;
-    off = align256v(off + sizeof(int) * (size_t)(max_items + 1));
+    L.item_desc = off;
+    off = align256v(off + sizeof(int4) * (size_t)(max_items + 1));
     L.counter = off;
     off = align256v(off + sizeof(int) * 4);
     L.tile_loss = off;
@@ -987,7 +1196,7 @@ static int bwd_gauss_grid() {
     if (cached) return cached;
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, vox_bwd_gauss_kernel<C, LOSS>, kBwdWarps * 32, 0);
+            &per_sm, vox_bwd_gauss_kernel<C, LOSS>, kBwdWarps * 32, 0);
     int dev = 0, sms = kSMs;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -996,23 +1205,23 @@ static int bwd_gauss_grid() {
 }
 
 template <int C, bool LOSS>
-static void bwd_launch(cudaStream_t stream, const Geom &g, const int2 *bins,
-                       const int *ids, const float4 *rec, const float2 *cq,
-                       const float *grad, const int2 *ib, const int *item_tile,
-                       const long long *total, int *counter, float *pos_grad,
-                       float *conic_grad, float *int_grad, const float *target,
+static void bwd_launch(cudaStream_t stream, const Geom &g, const int *ids,
+                       const float4 *rec, const float2 *cq, const float *grad,
+                       const int4 *item_desc, const long long *total,
+                       int *counter, float *pos_grad, float *conic_grad,
+                       float *int_grad, const float *target,
                        const float *grad_loss, float inv_denom) {
     vox_bwd_gauss_kernel<C, LOSS><<<bwd_gauss_grid<C, LOSS>(), kBwdWarps * 32,
                                     0, stream>>>(
-        g, bins, ids, rec, cq, grad, ib, item_tile, total, counter, pos_grad,
+        g, ids, rec, cq, grad, item_desc, total, counter, pos_grad,
         conic_grad, int_grad, target, grad_loss, inv_denom);
 }
 
 // Backward work plan from tile_bins: per-tile bucket counts, their scan and
-// the bucket -> tile map (the kernel's work queue).
+// the item descriptors (the kernel's work queue).
 static cudaError_t launch_bwd_plan(const int2 *bins, long long ntiles,
                                    int *item_counts, long long *partials,
-                                   int *item_bins, int *item_tile,
+                                   int *item_bins, int4 *item_desc,
                                    cudaStream_t stream) {
     const unsigned tblocks = (unsigned)((ntiles + 255) / 256);
     item_count_kernel<<<tblocks, 256, 0, stream>>>(bins, ntiles, item_counts);
@@ -1020,7 +1229,7 @@ static cudaError_t launch_bwd_plan(const int2 *bins, long long ntiles,
                                           item_bins, stream, LLONG_MAX);
     if (err) return err;
     item_fill_kernel<<<tblocks, 256, 0, stream>>>(
-        reinterpret_cast<const int2 *>(item_bins), ntiles, item_tile);
+        bins, reinterpret_cast<const int2 *>(item_bins), ntiles, item_desc);
     count_launches(2);
     return cudaGetLastError();
 }
@@ -1046,7 +1255,7 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     int *item_counts = reinterpret_cast<int *>(base + L.item_counts);
     int *item_bins = reinterpret_cast<int *>(base + L.item_bins);
     long long *partials = reinterpret_cast<long long *>(base + L.partials);
-    int *item_tile = reinterpret_cast<int *>(base + L.item_tile);
+    int4 *item_desc = reinterpret_cast<int4 *>(base + L.item_desc);
     int *counter = reinterpret_cast<int *>(base + L.counter);
     const long long nblocks = (ntiles + 4095) / 4096;
 
@@ -1056,7 +1265,7 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
         // records were built by the forward in this workspace; only plan
         if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
         return launch_bwd_plan(bins, ntiles, item_counts, partials, item_bins,
-                               item_tile, stream);
+                               item_desc, stream);
     }
     if (stage == kBwdPrepared) {
         zero_grads_kernel<<<std::max(1, std::min((n + 255) / 256, kSMs * 8)),
@@ -1073,17 +1282,16 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
         if ((err = cudaMemsetAsync(counter, 0, sizeof(int) * 4, stream))) return err;
         if ((err = launch_prep(n, C, pos_radii, conics, intens, rec, stream))) return err;
         if ((err = launch_bwd_plan(bins, ntiles, item_counts, partials,
-                                   item_bins, item_tile, stream)))
+                                   item_bins, item_desc, stream)))
             return err;
     }
     const long long *total = partials + nblocks;
     const float2 *cq = reinterpret_cast<const float2 *>(conics);
-    const int2 *ib = reinterpret_cast<const int2 *>(item_bins);
     const bool loss = target != nullptr;
     profile_mark(kProfBackwardGauss, false, stream);
 #define GSV_BWD(Cc, Ll)                                                       \
-    bwd_launch<Cc, Ll>(stream, g, bins, ids, rec, cq, grad, ib, item_tile,    \
-                       total, counter, pos_grad, conic_grad, int_grad, target, \
+    bwd_launch<Cc, Ll>(stream, g, ids, rec, cq, grad, item_desc, total,       \
+                       counter, pos_grad, conic_grad, int_grad, target,        \
                        grad_loss, inv_denom)
     switch (C * 2 + (loss ? 1 : 0)) {
         case 2: GSV_BWD(1, false); break;

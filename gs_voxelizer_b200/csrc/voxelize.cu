@@ -163,14 +163,19 @@ __device__ __forceinline__ float2 sigma_pair(float2 P, float2 L, float Cz,
     return __ffma2_rn(d, __ffma2_rn(f2(Cz), d, L), P);
 }
 
+// Accumulators acc[j][c] hold the lane's two columns, (x, y) in .x and
+// (x, y + 4) in .y, at z-offset j, so that they update as pairs.
+
+// Exact path: acc += I * alpha where thr <= s (and s <= 0 when CHECK_SIGN),
+// one compare and one predicated FMA per evaluation.
 template <int C, bool CHECK_SIGN>
-__device__ __forceinline__ void fwd_accumulate(float (&acc)[2][8][C], int j,
+__device__ __forceinline__ void fwd_accumulate(float2 (&acc)[8][C], int j,
                                                const float (&I)[C], float a0,
                                                float a1, float s0, float s1,
                                                float thr) {
     if (C == 1) {
-        fma_if_valid<CHECK_SIGN>(acc[0][j][0], I[0], a0, s0, thr);
-        fma_if_valid<CHECK_SIGN>(acc[1][j][0], I[0], a1, s1, thr);
+        fma_if_valid<CHECK_SIGN>(acc[j][0].x, I[0], a0, s0, thr);
+        fma_if_valid<CHECK_SIGN>(acc[j][0].y, I[0], a1, s1, thr);
     } else {
         bool ok0 = s0 >= thr, ok1 = s1 >= thr;
         if (CHECK_SIGN) {
@@ -179,24 +184,54 @@ __device__ __forceinline__ void fwd_accumulate(float (&acc)[2][8][C], int j,
         }
 #pragma unroll
         for (int c = 0; c < C; ++c) {
-            if (ok0) acc[0][j][c] = fmaf(I[c], a0, acc[0][j][c]);
-            if (ok1) acc[1][j][c] = fmaf(I[c], a1, acc[1][j][c]);
+            if (ok0) acc[j][c].x = fmaf(I[c], a0, acc[j][c].x);
+            if (ok1) acc[j][c].y = fmaf(I[c], a1, acc[j][c].y);
         }
     }
 }
 
-// One exponential per evaluation.
+// Flush path (robustly positive-definite Gaussians, -126 <= thr <= -1):
+// m = alpha * cm with cm = 2^(-thr - 126) is below the smallest normal
+// float, and flushed to exactly 0, precisely when alpha < 2^thr (the cull);
+// acc += m * Is with Is = I * 2^(thr + 126) restores the scale. Two
+// evaluations per paired instruction, no compare.
+template <int C>
+__device__ __forceinline__ void fwd_accumulate_flush(float2 (&acc)[8][C],
+                                                     int j,
+                                                     const float2 (&Is)[C],
+                                                     float2 a, float2 cm) {
+    const float2 m = fmul2_ftz(a, cm);
+#pragma unroll
+    for (int c = 0; c < C; ++c) acc[j][c] = ffma2_ftz(m, Is[c], acc[j][c]);
+}
+
+// One exponential per evaluation, exact cull.
 template <int C, bool CHECK_SIGN>
 __device__ __forceinline__ void fwd_pair_direct(float2 P, float2 L, float Cz,
                                                 float thr,
                                                 const float (&dz)[8],
                                                 const float (&I)[C],
-                                                float (&acc)[2][8][C]) {
+                                                float2 (&acc)[8][C]) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const float2 s = sigma_pair(P, L, Cz, dz[j]);
         fwd_accumulate<C, CHECK_SIGN>(acc, j, I, ex2(s.x), ex2(s.y), s.x, s.y,
                                       thr);
+    }
+}
+
+// One exponential per evaluation, flush-mask cull.
+template <int C>
+__device__ __forceinline__ void fwd_pair_direct_flush(float2 P, float2 L,
+                                                      float Cz, float2 cm,
+                                                      const float (&dz)[8],
+                                                      const float2 (&Is)[C],
+                                                      float2 (&acc)[8][C]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float2 s = sigma_pair(P, L, Cz, dz[j]);
+        fwd_accumulate_flush<C>(acc, j, Is, make_float2(ex2(s.x), ex2(s.y)),
+                                cm);
     }
 }
 
@@ -208,29 +243,31 @@ __device__ __forceinline__ void fwd_pair_direct(float2 P, float2 L, float Cz,
 // point of a chain above the cull threshold implies the chain's anchor
 // exponent is >= -112 (concave quadratic, slope <= 2 sqrt(40 |Cz|)), so the
 // anchor never flushes to zero while a later point still counts, and the
-// products stay within ~10 ulp of the direct exponential. The cull test
-// compares alpha against athr = 2^thr.
+// products stay within ~10 ulp of the direct exponential. The chain runs
+// on unscaled alpha; the cull is the flush mask of fwd_accumulate_flush.
 template <int C>
 __device__ __forceinline__ void fwd_pair_chain(float2 P, float2 L, float Cz,
-                                               float q, float athr,
+                                               float q, float2 cm,
                                                const float (&dz)[8],
-                                               const float (&I)[C],
-                                               float (&acc)[2][8][C]) {
+                                               const float2 (&Is)[C],
+                                               float2 (&acc)[8][C]) {
 #pragma unroll
     for (int seg = 0; seg < 8; seg += 4) {
         const float2 s0 = sigma_pair(P, L, Cz, dz[seg]);
         const float2 s1 = sigma_pair(P, L, Cz, dz[seg + 1]);
         const float2 d = __ffma2_rn(s0, f2(-1.f), s1);
         float2 a = make_float2(ex2(s0.x), ex2(s0.y));
-        float2 r = make_float2(ex2(d.x), ex2(d.y));
+        // s <= 0 (robust), so a step ratio above 2^126 only follows an
+        // anchor that flushed to 0; the clamp keeps that chain at 0 * finite
+        // (the flush mask does not discard NaN as a compare would)
+        float2 r = make_float2(ex2(fminf(d.x, 126.f)), ex2(fminf(d.y, 126.f)));
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             if (k > 0) {
                 a = __fmul2_rn(a, r);
                 if (k < 3) r = __fmul2_rn(r, f2(q));
             }
-            fwd_accumulate<C, false>(acc, seg + k, I, a.x, a.y, a.x, a.y,
-                                     athr);
+            fwd_accumulate_flush<C>(acc, seg + k, Is, a, cm);
         }
     }
 }
@@ -244,7 +281,7 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                float *__restrict__ out, const float *__restrict__ target,
                float *__restrict__ tile_loss) {
     constexpr int R = Rec<C>::kF4;
-    constexpr int RS = R + 3;  // record + 8 dz + (q, athr, fast)
+    constexpr int RS = R + 3;  // record + 8 dz + (q, cm, mode, 1 / cm)
     constexpr int kStage = (kFwdBatch * RS * 4 > kTileVoxels * C)
                                ? kFwdBatch * RS * 4
                                : kTileVoxels * C;
@@ -258,13 +295,11 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
     const int lx = lane & 7, ly = lane >> 3;
     const float fx = lx + 0.5f, fy = ly + 0.5f;
 
-    float acc[2][8][C];
+    float2 acc[8][C];
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
+    for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-            for (int c = 0; c < C; ++c) acc[k][j][c] = 0.f;
+        for (int c = 0; c < C; ++c) acc[j][c] = make_float2(0.f, 0.f);
 
     const int2 range = bins[tile];
     for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
@@ -283,11 +318,16 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                                          r0.z - 3.5f);
             sb[k * RS + R + 1] = make_float4(r0.z - 4.5f, r0.z - 5.5f,
                                              r0.z - 6.5f, r0.z - 7.5f);
+            // per-Gaussian mode: 2 chain + flush mask, 1 direct + flush
+            // mask, 0 exact compare (not robust, or thr out of range)
             const float Cz = sb[k * RS + 1].z, thr = r0.w;
-            const bool fast = robust_flag(thr) && Cz >= -2.f && thr >= -40.f &&
-                              thr <= 128.f;
+            const bool flush =
+                robust_flag(thr) && thr >= -126.f && thr <= -1.f;
+            const bool chain = flush && Cz >= -2.f && thr >= -40.f;
+            const float cm = flush ? ex2(-thr - 126.f) : 0.f;
             sb[k * RS + R + 2] =
-                make_float4(ex2(2.f * Cz), ex2(thr), fast ? 1.f : 0.f, 0.f);
+                make_float4(ex2(2.f * Cz), cm, chain ? 2.f : (flush ? 1.f : 0.f),
+                            flush ? 1.f / cm : 0.f);
         }
         __syncwarp();
 #pragma unroll 1
@@ -308,9 +348,15 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                 f2(dx), __ffma2_rn(f2(r1.w), dy, f2(r1.x * dx)),
                 __fmul2_rn(__fmul2_rn(f2(r1.y), dy), dy));
             const float2 L = __ffma2_rn(f2(r2.y), dy, f2(r2.x * dx));
-            if (ex.z != 0.f)
-                fwd_pair_chain<C>(P, L, r1.z, ex.x, ex.y, dz, I, acc);
-            else if (robust_flag(r0.w))
+            if (ex.z != 0.f) {
+                float2 Is[C];
+#pragma unroll
+                for (int c = 0; c < C; ++c) Is[c] = f2(I[c] * ex.w);
+                if (ex.z == 2.f)
+                    fwd_pair_chain<C>(P, L, r1.z, ex.x, f2(ex.y), dz, Is, acc);
+                else
+                    fwd_pair_direct_flush<C>(P, L, r1.z, f2(ex.y), dz, Is, acc);
+            } else if (robust_flag(r0.w))
                 fwd_pair_direct<C, false>(P, L, r1.z, r0.w, dz, I, acc);
             else
                 fwd_pair_direct<C, true>(P, L, r1.z, r0.w, dz, I, acc);
@@ -325,7 +371,8 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
         for (int j = 0; j < 8; ++j)
 #pragma unroll
             for (int c = 0; c < C; ++c)
-                smem[((j * 64) + (ly + 4 * k) * 8 + lx) * C + c] = acc[k][j][c];
+                smem[((j * 64) + (ly + 4 * k) * 8 + lx) * C + c] =
+                    k == 0 ? acc[j][c].x : acc[j][c].y;
     __syncwarp();
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                         (!LOSS || (reinterpret_cast<uintptr_t>(target) & 15) == 0);

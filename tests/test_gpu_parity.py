@@ -45,6 +45,12 @@ def assert_vol_close(got, ref):
     assert not bad.any(), (
         f"{bad.sum()} of {bad.size} voxels out of tolerance, max err "
         f"{err.max():.3e}")
+    # where every contribution is culled the voxel is exactly zero (the
+    # kernels cull by flushing to zero; a contribution exactly at the
+    # threshold may fall either way, so allow a few)
+    zero = ref == 0
+    stray = int((got[zero] != 0).sum())
+    assert stray <= max(2, zero.sum() // 10000), (stray, int(zero.sum()))
 
 
 def assert_grad_close(got, ref, what):

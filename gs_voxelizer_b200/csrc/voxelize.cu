@@ -39,6 +39,7 @@ cudaError_t launch_sum(long long n, const float *a, const float *b,
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 template <int C>
 struct Rec {
@@ -755,7 +756,6 @@ __device__ __forceinline__ void bwd_item(const float *buf, int K,
                                          const ItemLanes &L, int gid,
                                          const float4 &r0, const float4 &r1,
                                          const float4 &r2, const float4 &r3,
-                                         const float2 *__restrict__ conics,
                                          float *__restrict__ pos_grad,
                                          float *__restrict__ conic_grad,
                                          float *__restrict__ int_grad) {
@@ -842,13 +842,14 @@ __device__ __forceinline__ void bwd_item(const float *buf, int K,
 #pragma unroll
         for (int c = 0; c < C; ++c) W[c] *= corr;
         const float k = ((C == 1) ? I[0] : 1.f) * corr;  // sigma_grad = I * w
-        const float2 ab = conics[3 * gid + 0], cd = conics[3 * gid + 1],
-                     ef = conics[3 * gid + 2];
-        const float a_ = ab.x, b_ = ab.y, c_ = cd.x, d_ = cd.y, e_ = ef.x,
-                    f_ = ef.y;
+        // -Q (conic) from the record: r1 = (h a, h d, h f, -log2e b),
+        // r2 = (-log2e c, -log2e e, ..) with h = -log2e / 2
+        const float nqa = 2.f * kLn2 * r1.x, nqd = 2.f * kLn2 * r1.y,
+                    nqf = 2.f * kLn2 * r1.z, nqb = kLn2 * r1.w,
+                    nqc = kLn2 * r2.x, nqe = kLn2 * r2.y;
         const float vx = k * Vx, vy = k * Vy, vz = k * Vz;
-        red_add4(pos_grad + 4 * (size_t)gid, -(a_ * vx + b_ * vy + c_ * vz),
-                 -(b_ * vx + d_ * vy + e_ * vz), -(c_ * vx + e_ * vy + f_ * vz),
+        red_add4(pos_grad + 4 * (size_t)gid, nqa * vx + nqb * vy + nqc * vz,
+                 nqb * vx + nqd * vy + nqe * vz, nqc * vx + nqe * vy + nqf * vz,
                  0.f);
         float *cg = conic_grad + 6 * (size_t)gid;
         red_add2(cg + 0, -0.5f * k * Sxx, -k * Sxy);
@@ -923,16 +924,17 @@ vox_bwd_gauss_kernel(Geom g, const int *__restrict__ ids,
         const ItemLanes L = item_lanes(d.z, lane);
         int ox, oy, oz;
         tile_coords(g, d.x, ox, oy, oz);
+        // records first: their loads are in flight while the tile stages
+        const int gid = L.valid ? __ldg(ids + d.y + L.gi) : 0;
+        float4 r0, r1, r2, r3;
+        item_record<R>(rec, gid, L.valid, ox, oy, oz, r0, r1, r2, r3);
         __syncwarp();
         const int K = stage_grad_tile<C, LOSS>(g, grad, target, scale, ox, oy,
                                                oz, buf, lane);
         __syncwarp();
         if (K == INT_MIN) continue;  // dL/dvol is zero on this tile
-        const int gid = L.valid ? ids[d.y + L.gi] : 0;
-        float4 r0, r1, r2, r3;
-        item_record<R>(rec, gid, L.valid, ox, oy, oz, r0, r1, r2, r3);
-        bwd_item<C>(buf, K, L, gid, r0, r1, r2, r3, conics, pos_grad,
-                    conic_grad, int_grad);
+        bwd_item<C>(buf, K, L, gid, r0, r1, r2, r3, pos_grad, conic_grad,
+                    int_grad);
     }
 }
 

@@ -71,7 +71,8 @@ SIGNATURES = {
     "gsv_voxelize_l1_workspace_bytes": (_SZ, [_I32, _I32, _I64, _I3, _I32, _I32]),
     "gsv_voxelize_forward_l1": (
         ctypes.c_int, [_I3, _I32, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P,
-                       _P, ctypes.c_float, _P, _P, _P, _P, _P, _SZ, _P]),
+                       _P, ctypes.c_float, _P, _P, _P, _P, _P, _P, _P, _SZ,
+                       _P]),
     "gsv_voxelize_backward_per_gaussian_l1": (
         ctypes.c_int, [_I3, _I32, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P,
                        _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _SZ, _P]),

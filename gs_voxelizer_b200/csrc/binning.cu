@@ -23,8 +23,8 @@ namespace gsv {
 namespace {
 
 constexpr int kScanThreads = 256;
-constexpr int kScanItems = 16;
-constexpr int kScanTile = kScanThreads * kScanItems;  // 4096
+constexpr int kScanItems = 2;
+constexpr int kScanTile = kScanThreads * kScanItems;  // 512
 
 struct Box {
     int x0, y0, z0, nx, ny, nz;
@@ -150,66 +150,111 @@ __device__ __forceinline__ long long block_excl_scan_ll(long long v,
     return warp_prefix + incl - v;
 }
 
-template <typename T>
+// Work items of the per-Gaussian backward for a tile of c pairs.
+__device__ __forceinline__ int tile_items(int c) { return (c + 31) >> 5; }
+
+// partials[b] = sum of block b's counts; with ipartials, ipartials[b] = sum
+// of its work items (the backward's plan, scanned alongside the pairs)
 __global__ void __launch_bounds__(kScanThreads)
-scan_partials_kernel(const T *__restrict__ in, long long n,
-                     long long *__restrict__ partials) {
+scan_partials_kernel(const int *__restrict__ in, long long n,
+                     long long *__restrict__ partials,
+                     long long *__restrict__ ipartials) {
     __shared__ long long smem[32];
     const long long base = (long long)blockIdx.x * kScanTile;
-    long long s = 0;
+    long long s = 0, si = 0;
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k) {
         const long long i = base + (long long)k * kScanThreads + threadIdx.x;
-        if (i < n) s += (long long)in[i];
+        if (i < n) {
+            const int c = in[i];
+            s += c;
+            si += tile_items(c);
+        }
     }
     s = block_reduce_ll(s, smem);
     if (threadIdx.x == 0) partials[blockIdx.x] = s;
+    if (ipartials) {
+        si = block_reduce_ll(si, smem);
+        if (threadIdx.x == 0) ipartials[blockIdx.x] = si;
+    }
 }
 
-// single CTA: exclusive scan of the per-block partial sums in place, and the
-// grand total into partials[nblocks]
-__global__ void __launch_bounds__(1024)
-scan_partials_top_kernel(long long *__restrict__ partials, int nblocks) {
-    __shared__ long long smem[32];
+// exclusive scan of p[0..nblocks) in place, grand total (clamped to
+// total_cap) into p[nblocks]; returns the unclamped total
+__device__ __forceinline__ long long scan_partials_block(long long *p,
+                                                         int nblocks,
+                                                         long long *smem,
+                                                         long long total_cap) {
     const int per = (nblocks + 1023) / 1024;
     const int begin = threadIdx.x * per;
     long long local = 0;
     for (int k = 0; k < per; ++k)
-        if (begin + k < nblocks) local += partials[begin + k];
+        if (begin + k < nblocks) local += p[begin + k];
     long long total;
     long long run = block_excl_scan_ll(local, smem, &total);
     for (int k = 0; k < per; ++k) {
         if (begin + k < nblocks) {
-            const long long v = partials[begin + k];
-            partials[begin + k] = run;
+            const long long v = p[begin + k];
+            p[begin + k] = run;
             run += v;
         }
     }
-    if (threadIdx.x == 0) partials[nblocks] = total;
+    if (threadIdx.x == 0) p[nblocks] = min(total, total_cap);
+    return total;
+}
+
+// single CTA: exclusive scans of the per-block partial sums (pairs, and
+// items when given); the pair total also to count_out, with overflow_out =
+// (total > cap). The item total is clamped to icap (the item buffer), as
+// the item ranges are, so the backward never reads past the descriptors.
+__global__ void __launch_bounds__(1024)
+scan_partials_top_kernel(long long *__restrict__ partials,
+                         long long *__restrict__ ipartials, int nblocks,
+                         long long cap, long long icap,
+                         long long *__restrict__ count_out,
+                         float *__restrict__ overflow_out) {
+    __shared__ long long smem[32];
+    const long long total =
+        scan_partials_block(partials, nblocks, smem, LLONG_MAX);
+    if (threadIdx.x == 0) {
+        if (count_out) *count_out = total;
+        if (overflow_out) *overflow_out = total > cap ? 1.f : 0.f;
+    }
+    if (ipartials) {
+        __syncthreads();
+        scan_partials_block(ipartials, nblocks, smem, icap);
+    }
 }
 
 // tile_bins[t] = count ? (offset, offset + count) : (0, 0); cursor[t] = offset.
 // Offsets and ends are clamped to `cap` (the id buffer's capacity): when the
 // pairs outnumber the buffer, every range still lies inside it, the scatter
 // drops what does not fit, and the caller detects the overflow from the count.
+// With ipartials, item_bins[t] = the tile's range of work items, clamped to
+// icap (the item buffer) in the same way.
 __global__ void __launch_bounds__(kScanThreads)
 scan_bins_kernel(const int *__restrict__ counts, long long n,
                  const long long *__restrict__ partials,
                  int2 *__restrict__ tile_bins, int *__restrict__ cursor,
-                 long long cap) {
+                 long long cap, const long long *__restrict__ ipartials,
+                 int2 *__restrict__ item_bins, long long icap) {
     __shared__ long long smem[32];
     const long long base = (long long)blockIdx.x * kScanTile;
     // each thread owns kScanItems consecutive tiles
     const long long first = base + (long long)threadIdx.x * kScanItems;
     int v[kScanItems];
-    long long s = 0;
+    long long s = 0, si = 0;
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k) {
         v[k] = (first + k < n) ? counts[first + k] : 0;
         s += v[k];
+        si += tile_items(v[k]);
     }
     long long total;
     long long run = block_excl_scan_ll(s, smem, &total) + partials[blockIdx.x];
+    long long irun = 0;
+    if (ipartials)
+        irun = block_excl_scan_ll(si, smem, &total) + ipartials[blockIdx.x];
 #pragma unroll
     for (int k = 0; k < kScanItems; ++k) {
         if (first + k < n) {
@@ -219,6 +264,12 @@ scan_bins_kernel(const int *__restrict__ counts, long long n,
                 v[k] > 0 ? make_int2(off, end) : make_int2(0, 0);
             cursor[first + k] = off;
             run += v[k];
+            if (ipartials) {
+                const int ni = tile_items(v[k]);
+                item_bins[first + k] = make_int2((int)min(irun, icap),
+                                                 (int)min(irun + ni, icap));
+                irun += ni;
+            }
         }
     }
 }
@@ -282,12 +333,24 @@ constexpr int kCtaSortMax = 16384;
 __global__ void __launch_bounds__(256)
 sort_segments_warp_kernel(const int2 *__restrict__ tile_bins, long long ntiles,
                           int *__restrict__ ids, int *__restrict__ big_list,
-                          int *__restrict__ big_count) {
+                          int *__restrict__ big_count,
+                          const int2 *__restrict__ item_bins,
+                          int4 *__restrict__ item_desc) {
     const int lane = threadIdx.x & 31;
     const long long w0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
     for (long long t = w0; t < ntiles; t += nw) {
         const int2 r = tile_bins[t];
+        if (item_desc) {
+            // the backward's work items of this tile: (tile, first pair,
+            // Gaussians <= 32)
+            const int2 it = item_bins[t];
+            for (int k = it.x + lane; k < it.y; k += 32) {
+                const int start = r.x + 32 * (k - it.x);
+                item_desc[k] =
+                    make_int4((int)t, start, max(0, min(32, r.y - start)), 0);
+            }
+        }
         const int n = r.y - r.x;
         if (n <= 1) continue;
         int *seg = ids + r.x;
@@ -441,19 +504,32 @@ size_t bin_workspace_bytes(long long ntiles, long long nisect) {
     return bin_layout(ntiles, nisect).total;
 }
 
+long long scan_blocks(long long ntiles) {
+    return (ntiles + kScanTile - 1) / kScanTile;
+}
+
 // Exclusive scan of per-tile counts into tile_bins / cursors (counts is
-// overwritten with the cursors). Exposed for the backward planner too.
+// overwritten with the cursors), ranges clamped to `cap`; the grand total is
+// left in partials[scan_blocks(ntiles)] and, when given, in count_out, with
+// overflow_out = (total > cap). With `items` the backward's work items per
+// tile are scanned too (see ItemScan). Exposed for the backward planner.
 cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *partials, int *tile_bins,
-                                cudaStream_t stream, long long cap) {
-    const long long nblocks = (ntiles + kScanTile - 1) / kScanTile;
+                                cudaStream_t stream, long long cap,
+                                long long *count_out, float *overflow_out,
+                                const ItemScan *items) {
+    const long long nblocks = scan_blocks(ntiles);
     if (nblocks > 1024LL * 64) return cudaErrorInvalidValue;
-    scan_partials_kernel<int><<<(unsigned)nblocks, kScanThreads, 0, stream>>>(
-        counts, ntiles, partials);
-    scan_partials_top_kernel<<<1, 1024, 0, stream>>>(partials, (int)nblocks);
+    long long *ip = items ? items->partials : nullptr;
+    scan_partials_kernel<<<(unsigned)nblocks, kScanThreads, 0, stream>>>(
+        counts, ntiles, partials, ip);
+    scan_partials_top_kernel<<<1, 1024, 0, stream>>>(
+        partials, ip, (int)nblocks, cap, items ? items->cap : 0, count_out,
+        overflow_out);
     scan_bins_kernel<<<(unsigned)nblocks, kScanThreads, 0, stream>>>(
         counts, ntiles, partials, reinterpret_cast<int2 *>(tile_bins), counts,
-        cap);
+        cap, ip, items ? reinterpret_cast<int2 *>(items->item_bins) : nullptr,
+        items ? items->cap : 0);
     count_launches(3);
     return cudaGetLastError();
 }
@@ -461,7 +537,8 @@ cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
 cudaError_t launch_binning(int n, long long nisect, const int *tmin,
                            const int *tmax, int Tx, int Ty, int tz0, int tz1,
                            int *ids_out, int *tile_bins, void *ws,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, long long *count_out,
+                           float *overflow_out, const ItemScan *items) {
     const long long ntiles = (long long)(tz1 - tz0) * Ty * Tx;
     const BinLayout L = bin_layout(ntiles, nisect);
     char *base = static_cast<char *>(ws);
@@ -475,8 +552,16 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
     if ((err = cudaMemsetAsync(counts, 0, sizeof(int) * ntiles, stream)))
         return err;
     if ((err = cudaMemsetAsync(flags, 0, sizeof(int) * 4, stream))) return err;
-    if (ntiles == 0) return cudaSuccess;
-    if (n > 0 && nisect > 0) {
+    if (ntiles == 0) {
+        if (count_out &&
+            (err = cudaMemsetAsync(count_out, 0, sizeof(long long), stream)))
+            return err;
+        if (overflow_out &&
+            (err = cudaMemsetAsync(overflow_out, 0, sizeof(float), stream)))
+            return err;
+        return cudaSuccess;
+    }
+    if (n > 0 && (nisect > 0 || count_out || overflow_out)) {
         const int warps = (n + 31) / 32;
         const int blocks = min((warps + 7) / 8, kSMs * 16);
         expand_pairs_kernel<kCount><<<blocks, 256, 0, stream>>>(
@@ -484,7 +569,7 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
         count_launches(1);
     }
     if ((err = scan_counts_to_bins(counts, ntiles, partials, tile_bins, stream,
-                                   nisect)))
+                                   nisect, count_out, overflow_out, items)))
         return err;
     if (n <= 0 || nisect <= 0) return cudaGetLastError();
     {
@@ -500,7 +585,9 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
             std::min<long long>((warps_needed + 7) / 8, (long long)kSMs * 32);
         sort_segments_warp_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
             reinterpret_cast<const int2 *>(tile_bins), ntiles, ids_out,
-            big_list, flags);
+            big_list, flags,
+            items ? reinterpret_cast<const int2 *>(items->item_bins) : nullptr,
+            items ? items->desc : nullptr);
     }
     sort_segments_cta_kernel<<<kSMs * 2, 1024, kCtaSortMax * sizeof(int),
                                stream>>>(

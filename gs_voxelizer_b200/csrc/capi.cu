@@ -28,13 +28,18 @@ size_t bin_workspace_bytes(long long ntiles, long long nisect);
 cudaError_t launch_binning(int n, long long nisect, const int *tmin,
                            const int *tmax, int Tx, int Ty, int tz0, int tz1,
                            int *ids_out, int *tile_bins, void *ws,
-                           cudaStream_t stream);
+                           cudaStream_t stream, long long *count_out = nullptr,
+                           float *overflow_out = nullptr,
+                           const ItemScan *items = nullptr);
+ItemScan vox_item_scan(void *ws, long long n, int C, long long ntiles,
+                       long long nisect);
 cudaError_t launch_count_slab_pairs(int n, const int *tmin, const int *tmax,
                                     int tz0, int tz1, long long *out,
                                     cudaStream_t stream);
 size_t vox_workspace_bytes(long long n, int channels, long long ntiles,
                            long long nisect);
-cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
+                               const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
                                float *out, void *ws, cudaStream_t stream,
@@ -218,7 +223,7 @@ int forward_impl(const char *fn, const gsv::Geom &g, int32_t C, int32_t n,
                                            as_stream(stream)),
                            fn);
     }
-    return cuda_status(gsv::launch_vox_forward(g, C, n, ids, bins, pos, con,
+    return cuda_status(gsv::launch_vox_forward(g, C, n, nisect, ids, bins, pos, con,
                                                inten, out, ws,
                                                as_stream(stream), nullptr,
                                                nullptr, 1.0),
@@ -527,8 +532,9 @@ int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
                             const float *pos, const float *con,
                             const float *inten, const float *target,
                             float denom, int32_t *ids_out, int32_t *bins_out,
-                            float *out, float *loss_out, void *ws,
-                            size_t ws_bytes, void *stream) {
+                            float *out, float *loss_out, int64_t *count_out,
+                            float *overflow_out, void *ws, size_t ws_bytes,
+                            void *stream) {
     const char *fn = "gsv_voxelize_forward_l1";
     if (!check_vol(vol, fn)) return GSV_ERR_INVALID_ARGUMENT;
     const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
@@ -559,9 +565,13 @@ int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
     char *bin_ws = static_cast<char *>(ws);
     char *vox_ws = bin_ws + l1_bin_part(g, nisect);
     gsv::enable_large_smem();
-    cudaError_t err = gsv::launch_binning(n, nisect, tile_min, tile_max, g.Tx,
-                                          g.Ty, g.tz0, g.tz1, ids_out, bins_out,
-                                          bin_ws, s);
+    // the binning also scans and writes the backward's work plan
+    const gsv::ItemScan items =
+        gsv::vox_item_scan(vox_ws, n, C, g.slab_tiles(), nisect);
+    cudaError_t err = gsv::launch_binning(
+        n, nisect, tile_min, tile_max, g.Tx, g.Ty, g.tz0, g.tz1, ids_out,
+        bins_out, bin_ws, s, reinterpret_cast<long long *>(count_out),
+        overflow_out, &items);
     if (err) return cuda_status(err, fn);
     if (nisect == 0) {
         // empty volume: loss = sum |target| / denom
@@ -572,16 +582,10 @@ int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
                                                 vox_ws, s),
                            fn);
     }
-    err = gsv::launch_vox_forward(g, C, n, ids_out, bins_out, pos, con, inten,
+    err = gsv::launch_vox_forward(g, C, n, nisect, ids_out, bins_out, pos, con, inten,
                                   out, vox_ws, s, target, loss_out,
                                   1.0 / (double)denom);
-    if (err) return cuda_status(err, fn);
-    // plan the backward's work queue now, while the tile ranges are at hand
-    return cuda_status(gsv::launch_vox_backward_gauss(
-                           g, C, n, nisect, ids_out, bins_out, pos, con, inten,
-                           out, nullptr, nullptr, nullptr, vox_ws, s, target,
-                           nullptr, 1.f, gsv::kBwdPlanOnly),
-                       fn);
+    return cuda_status(err, fn);
 }
 
 int gsv_voxelize_backward_per_gaussian_l1(

@@ -46,10 +46,25 @@ inline Geom make_geom(const int32_t vol_zyx[3], int tz0 = 0, int tz1 = -1) {
 // Running count of kernels this library has launched (gsv_launch_count()).
 void count_launches(int k);
 
-// Stages of launch_vox_backward_gauss: everything; only the work plan (the
-// forward already built the records in the workspace); only the kernel (a
-// previous kBwdPlanOnly call prepared the workspace).
-enum BwdStage { kBwdFull = 0, kBwdPlanOnly = 1, kBwdPrepared = 2 };
+// Blocks of the tile scans (binning, backward plan) for ntiles tiles; the
+// scans leave their grand total at partials[scan_blocks(ntiles)].
+long long scan_blocks(long long ntiles);
+
+// The per-Gaussian backward's work plan, built while binning (fused-L1
+// forward): per-tile work-item ranges `item_bins` (int2 per tile), the scan
+// partials of the item counts (total in partials[scan_blocks(ntiles)]), the
+// item descriptors (tile, first pair, Gaussians) and the item buffer's
+// capacity, to which ranges are clamped.
+struct ItemScan {
+    long long *partials;
+    int *item_bins;
+    int4 *desc;
+    long long cap;
+};
+
+// Stages of launch_vox_backward_gauss: everything, or only the kernel (the
+// fused-L1 forward left the records and the work plan in the workspace).
+enum BwdStage { kBwdFull = 0, kBwdPrepared = 2 };
 
 // Optional CUDA events recorded right before / after the main voxelization
 // kernels (gsv_profile_kernel()); no-ops unless a caller installed events.

@@ -9,7 +9,8 @@
 // each tile, so dL/dvol is never written to HBM).
 //
 // Reductions are deterministic: fixed grid for a given size, per-block sums
-// in double, then one block summing the partials in order.
+// in double, then one block summing the partials in order (one block alone
+// for up to 64K elements).
 #include "common.cuh"
 
 namespace gsv {
@@ -83,6 +84,31 @@ finish_sum_kernel(const double *__restrict__ partial, int nparts,
     if (threadIdx.x == 0) out[0] = (float)(t * inv_denom);
 }
 
+// Small inputs: one CTA of 1024 threads, thread t summing elements t,
+// t + 1024, ... in order (coalesced), then a block sum: out[0] = sum *
+// inv_denom in one launch.
+constexpr int kSmallSumThreads = 1024;
+constexpr long long kSmallSum = 64 * 1024;
+
+__global__ void __launch_bounds__(kSmallSumThreads)
+sum_small_kernel(long long n, const float *__restrict__ a,
+                 const float *__restrict__ b, double inv_denom,
+                 float *__restrict__ out) {
+    __shared__ double smem[32];
+    float s = 0.f;
+    if (b) {
+#pragma unroll 8
+        for (long long i = threadIdx.x; i < n; i += kSmallSumThreads)
+            s += fabsf(a[i] - b[i]);
+    } else {
+#pragma unroll 8
+        for (long long i = threadIdx.x; i < n; i += kSmallSumThreads)
+            s += a[i];
+    }
+    const double t = block_sum_d((double)s, smem);
+    if (threadIdx.x == 0) out[0] = (float)(t * inv_denom);
+}
+
 // grad = sign(vol - target) * (*grad_loss) * inv_denom
 __global__ void __launch_bounds__(kRedThreads)
 l1_grad_kernel(long long n, const float *__restrict__ vol,
@@ -127,6 +153,12 @@ size_t l1_workspace_bytes(long long n) {
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
                        cudaStream_t stream) {
+    if (n <= kSmallSum) {
+        sum_small_kernel<<<1, kSmallSumThreads, 0, stream>>>(n, a, b,
+                                                             inv_denom, out);
+        count_launches(1);
+        return cudaGetLastError();
+    }
     const int blocks = reduce_blocks(n);
     double *partial = static_cast<double *>(ws);
     abs_diff_partials_kernel<<<blocks, kRedThreads, 0, stream>>>(n, a, b,

@@ -30,7 +30,8 @@
 #include "common.cuh"
 
 namespace gsv {
-cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
+                               const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
                                float *out, void *ws, cudaStream_t stream,
@@ -122,7 +123,7 @@ int gsv_voxelize_forward_noalloc(const int32_t vol[3], int32_t C, int32_t n,
         void *scratch = nullptr;
         err = scratch_address(&scratch);
         if (err == cudaSuccess)
-            err = gsv::launch_vox_forward(g, C, n, ids, bins, pos, con, inten,
+            err = gsv::launch_vox_forward(g, C, n, 0, ids, bins, pos, con, inten,
                                           out, scratch, s, nullptr, nullptr,
                                           1.0);
     }

@@ -30,7 +30,10 @@ namespace gsv {
 
 cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *partials, int *tile_bins,
-                                cudaStream_t stream, long long cap);
+                                cudaStream_t stream, long long cap,
+                                long long *count_out = nullptr,
+                                float *overflow_out = nullptr,
+                                const ItemScan *items = nullptr);
 size_t l1_workspace_bytes(long long n);
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
@@ -1133,7 +1136,7 @@ VoxLayout vox_layout(long long n, int channels, long long ntiles,
                      long long nisect) {
     VoxLayout L;
     const int R = channels <= 2 ? 3 : 4;
-    const long long nblocks = (ntiles + 4095) / 4096;
+    const long long nblocks = scan_blocks(ntiles);
     const long long max_items = (nisect + 31) / 32 + ntiles;
     size_t off = 0;
     L.rec = off;
@@ -1188,14 +1191,17 @@ static void fwd_launch(unsigned grid, cudaStream_t stream, const Geom &g,
 }
 
 // target != nullptr: fused L1, loss_out[0] = sum |vol - target| * inv_denom
-cudaError_t launch_vox_forward(const Geom &g, int C, int n, const int *ids,
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
+                               const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
                                float *out, void *ws, cudaStream_t stream,
                                const float *target, float *loss_out,
                                double inv_denom) {
     const long long ntiles = g.slab_tiles();
-    const VoxLayout L = vox_layout(n, C, ntiles, 0);
+    // the same layout as the backward's: the fused-L1 forward's binning has
+    // already written the backward's work plan into this workspace
+    const VoxLayout L = vox_layout(n, C, ntiles, nisect);
     char *base = static_cast<char *>(ws);
     float4 *rec = reinterpret_cast<float4 *>(base + L.rec);
     float *tile_loss = reinterpret_cast<float *>(base + L.tile_loss);
@@ -1283,6 +1289,20 @@ static cudaError_t launch_bwd_plan(const int2 *bins, long long ntiles,
     return cudaGetLastError();
 }
 
+// The work-plan buffers of the vox workspace, for the binning to fill
+// (ItemScan) in the fused-L1 forward.
+ItemScan vox_item_scan(void *ws, long long n, int C, long long ntiles,
+                       long long nisect) {
+    const VoxLayout L = vox_layout(n, C, ntiles, nisect);
+    char *base = static_cast<char *>(ws);
+    ItemScan it;
+    it.partials = reinterpret_cast<long long *>(base + L.partials);
+    it.item_bins = reinterpret_cast<int *>(base + L.item_bins);
+    it.desc = reinterpret_cast<int4 *>(base + L.item_desc);
+    it.cap = (nisect + 31) / 32 + ntiles;
+    return it;
+}
+
 // target != nullptr: fused L1; `grad` is then the forward volume and
 // dL/dvol = sign(vol - target) * grad_loss[0] * inv_denom.
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
@@ -1306,16 +1326,10 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     long long *partials = reinterpret_cast<long long *>(base + L.partials);
     int4 *item_desc = reinterpret_cast<int4 *>(base + L.item_desc);
     int *counter = reinterpret_cast<int *>(base + L.counter);
-    const long long nblocks = (ntiles + 4095) / 4096;
+    const long long nblocks = scan_blocks(ntiles);
 
     cudaError_t err;
     const int2 *bins = reinterpret_cast<const int2 *>(tile_bins);
-    if (stage == kBwdPlanOnly) {
-        // records were built by the forward in this workspace; only plan
-        if (n <= 0 || ntiles == 0 || nisect <= 0) return cudaSuccess;
-        return launch_bwd_plan(bins, ntiles, item_counts, partials, item_bins,
-                               item_desc, stream);
-    }
     if (stage == kBwdPrepared) {
         zero_grads_kernel<<<std::max(1, std::min((n + 255) / 256, kSMs * 8)),
                             256, 0, stream>>>(n, C, pos_grad, conic_grad,

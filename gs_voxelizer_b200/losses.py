@@ -102,7 +102,8 @@ class _VoxelizeL1(Function):
             tile_min.data_ptr(), tile_max.data_ptr(), _C._ptr(pos3d_radii),
             _C._ptr(conics), _C._ptr(intensities), _C._ptr(target),
             float(denom), _C._ptr(ids), _C._ptr(bins), _C._ptr(out),
-            loss.data_ptr(), ws.data_ptr(), ws.numel(), _C._stream(dev)))
+            loss.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
+            _C._stream(dev)))
         ctx.ws = ws
         ctx.plan, ctx.denom, ctx.group, ctx.one_d = plan, float(denom), group, one_d
         ctx.save_for_backward(pos3d_radii, conics, intensities, ids, bins, out,

@@ -174,7 +174,8 @@ class FusedL1Step:
             self.pos3d_radii.data_ptr(), self.conics.data_ptr(),
             inten.data_ptr(), _C._ptr(self.target), self.denom,
             _C._ptr(self.ids), _C._ptr(self.bins), _C._ptr(self.volume),
-            self.loss.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+            self.loss.data_ptr(), self.count.data_ptr(),
+            self.overflow.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
             self._stream()))
         check(lib.gsv_voxelize_backward_per_gaussian_l1(
             self._vol_c, p.tz0, p.tz1, self.C, self.n, self.capacity,
@@ -185,8 +186,6 @@ class FusedL1Step:
             self.grad_pos3d_radii.data_ptr(), self.grad_conics.data_ptr(),
             self.grad_intensities.data_ptr(), self.ws.data_ptr(),
             self.ws.numel(), self._stream()))
-        # overflow flag as a float, so the gradient all-reduce carries it
-        self.overflow.copy_(self.count > self.capacity)
 
     def _project_backward(self) -> None:
         pos, scale, quat, _ = self.params
@@ -202,8 +201,9 @@ class FusedL1Step:
         self._host.copy_(self.flat[-2:], non_blocking=True)
 
     def _part_a(self) -> None:
+        # the binning inside _voxelize writes the pair count and the
+        # overflow flag (a float, so that the gradient all-reduce carries it)
         self._project()
-        self._count()
         self._voxelize()
 
     def _part_b(self) -> None:

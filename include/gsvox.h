@@ -267,9 +267,11 @@ GSV_API int gsv_l1_loss_backward(int64_t n, const float *vol,
  * upper bound of it (a capacity), so that a step needs no host read of the
  * count: ids past the true count stay unused. If the true count exceeds
  * num_intersects, the tile ranges are clamped to it (no access outside the
- * buffers) and the results are invalid; the caller compares the count that
- * gsv_count_slab_intersects left in device memory and re-runs with a larger
- * capacity. Both calls of a step take the same num_intersects.
+ * buffers) and the results are invalid; the caller re-runs with a larger
+ * capacity. pair_count_out (nullable, device int64) receives the slab's true
+ * pair count and overflow_out (nullable, device float) 1.0 when it exceeds
+ * num_intersects, else 0.0, both computed during the binning. Both calls of
+ * a step take the same num_intersects.
  * No reference counterpart (fuses bindings.cu:261, :362 and :589 with the
  * loss the reference's callers compute in PyTorch).
  */
@@ -284,6 +286,7 @@ GSV_API int gsv_voxelize_forward_l1(
     const float *pos3d_radii, const float *conics, const float *intensities,
     const float *target, float denom, int32_t *gaussian_ids_sorted_out,
     int32_t *tile_bins_out, float *out_vol, float *loss_out,
+    int64_t *pair_count_out, float *overflow_out,
     void *workspace, size_t workspace_bytes, void *stream);
 
 GSV_API int gsv_voxelize_backward_per_gaussian_l1(

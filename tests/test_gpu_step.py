@@ -134,3 +134,23 @@ def test_step_on_a_slab():
     loss = step.run()
     assert loss == pytest.approx(want[0], rel=1e-5)
     _compare(step, params, want)
+
+
+@pytest.mark.parametrize("force_overflow", [False, True])
+def test_step_many_tiles(force_overflow):
+    """More than 64K tiles (136 x 512 x 512 voxels = 69 632 tiles): the
+    binning's multi-block scan path, including its pair count and overflow
+    flag."""
+    from gs_voxelizer_b200.workloads import phantom
+    cfg = K.small_config(vol=(136, 512, 512), n=3000, seed=74,
+                         scale=(0.002, 0.01))
+    target = phantom(cfg, device="cuda")
+    want = _autograd(cfg, target)
+    params, step = _step(cfg, target)
+    if force_overflow:
+        step._resize(0)
+    loss = step.run()
+    assert step.regrows == (1 if force_overflow else 0)
+    assert int(step.count.item()) <= step.capacity
+    assert loss == pytest.approx(want[0], rel=1e-5)
+    _compare(step, params, want)

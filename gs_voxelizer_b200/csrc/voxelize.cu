@@ -521,7 +521,7 @@ __device__ __forceinline__ int stage_grad_tile(const Geom &g,
         for (int x = 0; x < 8; ++x)
 #pragma unroll
             for (int c = 0; c < C; ++c)
-                buf[yl * S::kRow + x * S::kCol + zl * C + c] =
+                buf[yl * S::kRow + x * S::kCol + c * 8 + zl] =
                     v[h][x * C + c] * gk;
     }
     return K;
@@ -597,12 +597,12 @@ __device__ __forceinline__ RowSums bwd_row(const float *colbase, float mx,
             const float a = ok ? ex2(s) : 0.f;
             float w;
             {
-                float h = I[0] * gv[j * C];
+                float h = I[0] * gv[j];
 #pragma unroll
-                for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[j * C + c], h);
+                for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[c * 8 + j], h);
 #pragma unroll
                 for (int c = 0; c < C; ++c)
-                    W[c] = fmaf(a, gv[j * C + c], W[c]);
+                    W[c] = fmaf(a, gv[c * 8 + j], W[c]);
                 w = a * h;
             }
             T0 += w;
@@ -678,56 +678,76 @@ __device__ __forceinline__ RowSums bwd_row_flush1(const float *colbase,
     return r;
 }
 
-// Flush path for C > 1 (scalar): as bwd_row without the cull test.
+// Flush path for C > 1: as bwd_row_flush1, two z-voxels per paired
+// instruction; h = sum_c I_c dL/dvol_c and the channel sums W_c are kept as
+// (even z, odd z) pairs, collapsed by the caller.
 template <int C>
-__device__ __forceinline__ RowSums bwd_row_flush(const float *colbase,
-                                                 float mx, float A, float Cz,
-                                                 float E, float Dy, float By2s,
-                                                 float Fy,
-                                                 const float2 (&dzp)[4],
-                                                 const float2 (&dsp)[4],
-                                                 const float (&I)[C],
-                                                 float (&W)[C]) {
+__device__ __forceinline__ RowSums bwd_row_flushc(const float *colbase,
+                                                  float mx, float A, float Cz,
+                                                  float E, float Dy, float By2s,
+                                                  float Fy,
+                                                  const float2 (&dzp)[4],
+                                                  const float2 (&dsp)[4],
+                                                  const float (&I)[C],
+                                                  float2 (&W2)[C]) {
     using S = BwdSmem<C>;
-    RowSums r = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float2 z2 = f2(0.f), Cz2 = f2(Cz);
+    float2 R0 = z2, R1 = z2, R2 = z2, Rx0 = z2, Rxx = z2, Rx1 = z2;
 #pragma unroll
     for (int x = 0; x < 8; ++x) {
         const float dx = mx - ((float)x + 0.5f);
-        const float P = fmaf(dx, fmaf(A, dx, Dy), By2s);
-        const float L = fmaf(E, dx, Fy);
-        float gv[8 * C];
+        const float2 dx2 = f2(dx);
+        const float2 P = f2(fmaf(dx, fmaf(A, dx, Dy), By2s));
+        const float2 L = f2(fmaf(E, dx, Fy));
+        // dL/dvol of column x, [c][z]: 4 pairs per channel
+        float2 g[C][4];
 #pragma unroll
-        for (int q4 = 0; q4 < 2 * C; ++q4) {
-            const float4 t =
-                reinterpret_cast<const float4 *>(colbase + x * S::kCol)[q4];
-            gv[4 * q4 + 0] = t.x;
-            gv[4 * q4 + 1] = t.y;
-            gv[4 * q4 + 2] = t.z;
-            gv[4 * q4 + 3] = t.w;
+        for (int c = 0; c < C; ++c) {
+            const float4 ga =
+                reinterpret_cast<const float4 *>(colbase + x * S::kCol + c * 8)[0];
+            const float4 gb =
+                reinterpret_cast<const float4 *>(colbase + x * S::kCol + c * 8)[1];
+            g[c][0] = make_float2(ga.x, ga.y);
+            g[c][1] = make_float2(ga.z, ga.w);
+            g[c][2] = make_float2(gb.x, gb.y);
+            g[c][3] = make_float2(gb.z, gb.w);
         }
-        float T0 = 0.f, T1 = 0.f, T2 = 0.f;
+        float2 T0, T1, T2;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float dzj = pick(dzp, j), dsj = pick(dsp, j);
-            const float a = ex2(fmaf(dzj, fmaf(Cz, dzj, L), P));
-            float h = I[0] * gv[j * C];
+        for (int k = 0; k < 4; ++k) {
+            const float2 sp = __ffma2_rn(dzp[k], __ffma2_rn(Cz2, dzp[k], L), P);
+            const float2 a = make_float2(ex2(sp.x), ex2(sp.y));
+            float2 h = __fmul2_rn(f2(I[0]), g[0][k]);
 #pragma unroll
-            for (int c = 1; c < C; ++c) h = fmaf(I[c], gv[j * C + c], h);
+            for (int c = 1; c < C; ++c) h = __ffma2_rn(f2(I[c]), g[c][k], h);
 #pragma unroll
-            for (int c = 0; c < C; ++c) W[c] = fmaf(a, gv[j * C + c], W[c]);
-            const float w = a * h;
-            T0 += w;
-            T1 = fmaf(w, dzj, T1);
-            T2 = fmaf(w, dsj, T2);
+            for (int c = 0; c < C; ++c) W2[c] = __ffma2_rn(a, g[c][k], W2[c]);
+            const float2 w = __fmul2_rn(a, h);
+            if (k == 0) {
+                T0 = w;
+                T1 = __fmul2_rn(w, dzp[0]);
+                T2 = __fmul2_rn(w, dsp[0]);
+            } else {
+                T0 = __fadd2_rn(T0, w);
+                T1 = __ffma2_rn(w, dzp[k], T1);
+                T2 = __ffma2_rn(w, dsp[k], T2);
+            }
         }
-        r.R0 += T0;
-        r.R1 += T1;
-        r.R2 += T2;
-        const float u = dx * T0;
-        r.Rx0 += u;
-        r.Rxx = fmaf(u, dx, r.Rxx);
-        r.Rx1 = fmaf(dx, T1, r.Rx1);
+        R0 = __fadd2_rn(R0, T0);
+        R1 = __fadd2_rn(R1, T1);
+        R2 = __fadd2_rn(R2, T2);
+        const float2 u = __fmul2_rn(dx2, T0);
+        Rx0 = __fadd2_rn(Rx0, u);
+        Rxx = __ffma2_rn(u, dx2, Rxx);
+        Rx1 = __ffma2_rn(dx2, T1, Rx1);
     }
+    RowSums r;
+    r.R0 = R0.x + R0.y;
+    r.R1 = R1.x + R1.y;
+    r.R2 = R2.x + R2.y;
+    r.Rx0 = Rx0.x + Rx0.y;
+    r.Rxx = Rxx.x + Rxx.y;
+    r.Rx1 = Rx1.x + Rx1.y;
     return r;
 }
 
@@ -786,8 +806,12 @@ __device__ __forceinline__ void bwd_item(const float *buf, int K,
     float Sxx = 0.f, Syy = 0.f, Szz = 0.f, Sxy = 0.f, Sxz = 0.f, Syz = 0.f;
     float Vx = 0.f, Vy = 0.f, Vz = 0.f;
     float W[C];
+    float2 W2[C];  // flush path, C > 1: (even z, odd z) channel sums
 #pragma unroll
-    for (int c = 0; c < C; ++c) W[c] = 0.f;
+    for (int c = 0; c < C; ++c) {
+        W[c] = 0.f;
+        W2[c] = make_float2(0.f, 0.f);
+    }
 
 #pragma unroll 1
     for (int q = 0; q < L.rows; ++q) {
@@ -801,8 +825,8 @@ __device__ __forceinline__ void bwd_item(const float *buf, int K,
                 rs = bwd_row_flush1(colbase, r0.x, r1.x, r1.z, r2.x, Dy,
                                     By2 - shift, Fy, dzp, dsp);
             else
-                rs = bwd_row_flush<C>(colbase, r0.x, r1.x, r1.z, r2.x, Dy,
-                                      By2 - shift, Fy, dzp, dsp, I, W);
+                rs = bwd_row_flushc<C>(colbase, r0.x, r1.x, r1.z, r2.x, Dy,
+                                       By2 - shift, Fy, dzp, dsp, I, W2);
         } else if (all_robust) {
             rs = bwd_row<C, false>(colbase, r0.x, thr, r1.x, r1.z, r2.x, Dy,
                                    By2, Fy, dzp, dsp, I, W);
@@ -820,6 +844,11 @@ __device__ __forceinline__ void bwd_item(const float *buf, int K,
         Sxy = fmaf(dy, rs.Rx0, Sxy);
         Syz = fmaf(dy, rs.R1, Syz);
         Vy = fmaf(dy, rs.R0, Vy);
+    }
+
+    if (C > 1) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) W[c] += W2[c].x + W2[c].y;
     }
 
     // combine row groups (lanes gi, gi+gs, gi+2gs, ...)
@@ -897,7 +926,7 @@ __device__ __forceinline__ void item_record(const float4 *__restrict__ rec,
 // Per-Gaussian backward: persistent warps take items from an atomic
 // counter; each item stages its tile, loads its records and evaluates.
 template <int C, bool LOSS>
-__global__ void __launch_bounds__(kBwdWarps * 32, C == 1 ? 5 : (C == 2 ? 6 : 4))
+__global__ void __launch_bounds__(kBwdWarps * 32, C <= 2 ? 5 : 4)
 vox_bwd_gauss_kernel(Geom g, const int *__restrict__ ids,
                      const float4 *__restrict__ rec,
                      const float2 *__restrict__ conics,

@@ -63,20 +63,37 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
+    def _lines(self) -> int:
+        self.file.flush()
+        self.file.seek(0)
+        n = sum(1 for r in self.file.read().splitlines() if r.strip())
+        self.file.seek(0, 2)
+        return n
+
+    def _wait_for(self, n: int, limit_s: float) -> None:
+        t0 = time.time()
+        while time.time() - t0 < limit_s and self._lines() < n:
+            time.sleep(0.01)
+
     def start(self):
+        """Start sampling; returns once the first sample has arrived (so
+        that samples cover the timed region that follows)."""
         try:
             self.file = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
+            self._wait_for(1, 5.0)
+            self.n_before = self._lines()
         except Exception:
             self.proc = None
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.15)
+        # at least one sample taken after the timed region ended
+        self._wait_for(self.n_before + 2, 2.0)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)

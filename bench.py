@@ -7,8 +7,10 @@ backward), the path of the reference's own speed benchmark. Workload at
 N = 1 is BASELINE configuration 2: 256^3 volume, 100k Gaussians,
 64-ellipsoid phantom (synthetic, seeded). At N > 1 the volume is z-slab
 sharded with per-GPU work fixed (weak scaling): a (256N, 256, 256) volume
-with N x 100k Gaussians, one 256^3 slab per rank, one NCCL all-reduce of the
-per-Gaussian gradients per step.
+with N x 100k Gaussians, one 256^3 slab per rank; each rank owns the
+Gaussians whose centre lies in its slab and exchanges the boundary
+Gaussians (halo) with its peers, two NCCL all-to-alls per step
+(gs_voxelizer_b200.halo).
 
 Metric: Gaussian-voxel evaluations per second over the whole step, counting
 each (Gaussian, voxel) pair once in the forward and once in the backward
@@ -204,19 +206,34 @@ class Step:
             self.vox = voxelize.voxelize_gaussians
             self.vox_slab = slab.voxelize_gaussians_slab
             self.vox_l1 = losses.voxelize_gaussians_l1
-        # "graph": the sync-free step (step.FusedL1Step) replayed as a CUDA
-        # graph; "fused": the same kernels through autograd
-        # (losses.voxelize_gaussians_l1); "dropin": the reference-compatible
-        # voxelize_gaussians + torch L1
+        # "graph": the sync-free step replayed as CUDA graphs - on one GPU
+        # step.FusedL1Step, on several halo.HaloL1Step (each rank holds the
+        # Gaussians whose centre lies in its slab and exchanges the halo);
+        # "fused": the same kernels through autograd with replicated
+        # Gaussians (losses.voxelize_gaussians_l1); "dropin": the
+        # reference-compatible voxelize_gaussians + torch L1
         self.mode = "graph" if impl != "reference" else "dropin"
         self.fstep = None
+        self.step_host, self.step_in_bytes = self.host, self.in_bytes
         if impl != "reference":
-            from gs_voxelizer_b200.step import FusedL1Step
-            with torch.no_grad():
+            if world > 1:
+                from gs_voxelizer_b200.halo import HaloL1Step, owner_of
+                owners = owner_of(inputs[0], cfg.vol, cfg.world, cfg.center, world)
+                idx = np.nonzero(owners == rank)[0]
+                self.step_host = [torch.from_numpy(np.ascontiguousarray(a[idx])).pin_memory()
+                                  for a in inputs]
+                self.step_in_bytes = sum(h.numel() * h.element_size()
+                                         for h in self.step_host)
+                self.params = [h.to(dev) for h in self.step_host]
+                self.fstep = HaloL1Step(*self.params, cfg.vol, cfg.world,
+                                        cfg.center, self.target,
+                                        denom=self.nvox_global)
+            else:
+                from gs_voxelizer_b200.step import FusedL1Step
                 self.params = [h.to(dev) for h in self.host]
-            self.fstep = FusedL1Step(*self.params, cfg.vol, cfg.world,
-                                     cfg.center, self.target,
-                                     denom=self.nvox_global, plan=self.plan)
+                self.fstep = FusedL1Step(*self.params, cfg.vol, cfg.world,
+                                         cfg.center, self.target,
+                                         denom=self.nvox_global, plan=self.plan)
 
     def forward(self):
         cfg = self.cfg
@@ -267,7 +284,7 @@ class Step:
         """Public-API step with the inputs copied from pinned host memory and
         the loss read back to the host."""
         if self.mode == "graph":
-            for d, h in zip(self.params, self.host):
+            for d, h in zip(self.params, self.step_host):
                 d.copy_(h, non_blocking=True)
             return self.fstep.run()
         with torch.no_grad():
@@ -597,12 +614,16 @@ def main():
                    "gaussians": cfg.n, "channels": cfg.channels,
                    "intersections_per_gpu": n_isect,
                    "evals_per_step": evals_per_step,
-                   "parallelism": f"z-slab x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"z-slab x{world}, Gaussians owner-sharded with a "
+                                   "halo exchange" if world > 1 and impl != "reference"
+                                   else "single GPU"),
                    "l2": "flushed between timed steps (256 MB write)",
                    "loss": ("L1 vs phantom, torch l1_loss" if impl == "reference"
                             else "L1 vs phantom, fused into the voxelization "
                                  "kernels"),
                    "step": ("reference API through autograd" if impl == "reference"
+                            else "gs_voxelizer_b200.halo.HaloL1Step: sync-free, "
+                                 "3 CUDA graphs around 2 NCCL all-to-alls" if world > 1
                             else "gs_voxelizer_b200.step.FusedL1Step: sync-free, "
                                  "replayed as a CUDA graph")},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
@@ -611,7 +632,7 @@ def main():
         "autograd": autograd, "dropin": dropin,
         "e2e": {"value": evals_per_step / (e2e_ms / 1e3), "unit": UNIT,
                 "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": st.in_bytes,
+                "h2d_bytes_per_step": st.step_in_bytes if st.fstep is not None else st.in_bytes,
                 "d2h_bytes_per_step": 8 if st.fstep is not None else 4},
         "clocks": clocks,
     }

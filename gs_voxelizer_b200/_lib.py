@@ -78,7 +78,23 @@ SIGNATURES = {
                        _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, _SZ, _P]),
     "gsv_voxelize_forward_noalloc": (
         ctypes.c_int, [_I3, _I32, _I32, _I64, _P, _P, _P, _P, _P, _P, _P]),
+    "gsv_halo_workspace_bytes": (_SZ, [_I32, _I32]),
+    "gsv_halo_pack": (
+        ctypes.c_int, [_I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _P, _P,
+                       _P, _P, _P, _P, _SZ, _P]),
+    "gsv_halo_unpack": (
+        ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                       _P, _P]),
+    "gsv_halo_pack_grads": (
+        ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                       _P]),
+    "gsv_halo_accumulate": (
+        ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                       _P, _P]),
 }
+
+HALO_RECORD_FLOATS = 20
+HALO_GRAD_FLOATS = 16
 
 for _name, (_res, _args) in SIGNATURES.items():
     _fn = getattr(lib, _name)

@@ -33,6 +33,27 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
                            const ItemScan *items = nullptr);
 ItemScan vox_item_scan(void *ws, long long n, int C, long long ntiles,
                        long long nisect);
+size_t halo_workspace_bytes(int n, int world);
+cudaError_t launch_halo_pack(int n, int C, const float *pr, const float *cq,
+                             const float *inten, const int *tmin,
+                             const int *tmax, const HaloPeers &P, float *send,
+                             int *slot_map, long long *counts_out, void *ws,
+                             cudaStream_t stream);
+cudaError_t launch_halo_unpack(int n_own, int C, const HaloPeers &R,
+                               long long total_slots, const float *recv,
+                               float *pr, float *cq, float *inten, int *tmin,
+                               int *tmax, float *flags, cudaStream_t stream);
+cudaError_t launch_halo_pack_grads(int n_own, int C, const HaloPeers &R,
+                                   long long total_slots, const float *gp,
+                                   const float *gc, const float *gi,
+                                   const float *loss, const float *flags,
+                                   float *send, cudaStream_t stream);
+cudaError_t launch_halo_accumulate(int n, int C, const HaloPeers &P,
+                                   const int *slot_map, const float *recv,
+                                   float *gp, float *gc, float *gi,
+                                   const float *loss, const float *flags,
+                                   float *out, cudaStream_t stream);
+
 cudaError_t launch_count_slab_pairs(int n, const int *tmin, const int *tmax,
                                     int tz0, int tz1, long long *out,
                                     cudaStream_t stream);
@@ -262,6 +283,29 @@ int backward_impl(const char *fn, bool per_gaussian, const gsv::Geom &g,
 size_t l1_bin_part(const gsv::Geom &g, long long nisect) {
     return (gsv::bin_workspace_bytes(g.slab_tiles(), nisect) + 255) &
            ~size_t(255);
+}
+
+// halo exchange: per-peer description from the C arrays
+bool make_peers(int32_t world, int32_t rank, const int32_t *slab_tz,
+                const int64_t *seg_off, const int32_t *seg_slots,
+                gsv::HaloPeers &P, long long &total_slots) {
+    if (world < 1 || world > gsv::kHaloMaxRanks || rank < 0 || rank >= world ||
+        !seg_off || !seg_slots)
+        return false;
+    P.world = world;
+    P.rank = rank;
+    long long loff = 0;
+    for (int d = 0; d < world; ++d) {
+        P.tz0[d] = slab_tz ? slab_tz[2 * d] : 0;
+        P.tz1[d] = slab_tz ? slab_tz[2 * d + 1] : 0;
+        P.off[d] = seg_off[d];
+        P.cap[d] = d == rank ? 0 : seg_slots[d];
+        if (P.cap[d] < 0 || P.off[d] < 0) return false;
+        P.loff[d] = loff;
+        loff += P.cap[d];
+    }
+    total_slots = loff;
+    return true;
 }
 
 }  // namespace
@@ -620,6 +664,109 @@ int gsv_voxelize_backward_per_gaussian_l1(
                            out_vol, pos_grad, con_grad, int_grad, vox_ws,
                            as_stream(stream), target, grad_loss, 1.f / denom,
                            gsv::kBwdPrepared),
+                       fn);
+}
+
+size_t gsv_halo_workspace_bytes(int32_t n, int32_t world) {
+    if (n < 0 || world < 1 || world > gsv::kHaloMaxRanks) return 0;
+    return gsv::halo_workspace_bytes(n, world);
+}
+
+int gsv_halo_pack(int32_t n, int32_t C, const float *pos3d_radii,
+                          const float *conics, const float *intensities,
+                          const int32_t *tile_min, const int32_t *tile_max,
+                          int32_t world, int32_t rank, const int32_t *slab_tz,
+                          const int64_t *seg_off, const int32_t *seg_slots,
+                          float *send, int32_t *slot_map, int64_t *counts_out,
+                          void *ws, size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_halo_pack";
+    gsv::HaloPeers P;
+    long long total;
+    GSV_REQUIRE(n >= 0 && C >= 1 && C <= 4 && slab_tz &&
+                    make_peers(world, rank, slab_tz, seg_off, seg_slots, P, total),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
+    GSV_REQUIRE(ws && ws_bytes >= gsv::halo_workspace_bytes(n, world),
+                GSV_ERR_WORKSPACE_TOO_SMALL, "%s: workspace too small", fn);
+    GSV_REQUIRE(send && slot_map &&
+                    (n == 0 || (pos3d_radii && conics && intensities &&
+                                tile_min && tile_max)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(gsv::launch_halo_pack(n, C, pos3d_radii, conics,
+                                             intensities, tile_min, tile_max,
+                                             P, send, slot_map,
+                                             reinterpret_cast<long long *>(counts_out),
+                                             ws, as_stream(stream)),
+                       fn);
+}
+
+int gsv_halo_unpack(int32_t n_own, int32_t C, int32_t world,
+                            int32_t rank, const int64_t *seg_off,
+                            const int32_t *seg_slots, const float *recv,
+                            float *pos3d_radii, float *conics,
+                            float *intensities, int32_t *tile_min,
+                            int32_t *tile_max, float *flags, void *stream) {
+    const char *fn = "gsv_halo_unpack";
+    gsv::HaloPeers R;
+    long long total;
+    GSV_REQUIRE(n_own >= 0 && C >= 1 && C <= 4 &&
+                    make_peers(world, rank, nullptr, seg_off, seg_slots, R, total),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
+    GSV_REQUIRE(total == 0 || (recv && pos3d_radii && conics && intensities &&
+                               tile_min && tile_max && flags),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(gsv::launch_halo_unpack(n_own, C, R, total, recv,
+                                               pos3d_radii, conics, intensities,
+                                               tile_min, tile_max, flags,
+                                               as_stream(stream)),
+                       fn);
+}
+
+int gsv_halo_pack_grads(int32_t n_own, int32_t C, int32_t world,
+                                int32_t rank, const int64_t *seg_off,
+                                const int32_t *seg_slots,
+                                const float *pos3d_radii_grad,
+                                const float *conics_grad,
+                                const float *intensities_grad,
+                                const float *loss, const float *flags,
+                                float *send, void *stream) {
+    const char *fn = "gsv_halo_pack_grads";
+    gsv::HaloPeers R;
+    long long total;
+    GSV_REQUIRE(n_own >= 0 && C >= 1 && C <= 4 &&
+                    make_peers(world, rank, nullptr, seg_off, seg_slots, R, total),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
+    GSV_REQUIRE(send && loss && flags &&
+                    (total == 0 || (pos3d_radii_grad && conics_grad &&
+                                    intensities_grad)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(gsv::launch_halo_pack_grads(
+                           n_own, C, R, total, pos3d_radii_grad, conics_grad,
+                           intensities_grad, loss, flags, send,
+                           as_stream(stream)),
+                       fn);
+}
+
+int gsv_halo_accumulate(int32_t n, int32_t C, int32_t world,
+                                int32_t rank, const int64_t *seg_off,
+                                const int32_t *slot_map, const float *recv,
+                                float *pos3d_radii_grad, float *conics_grad,
+                                float *intensities_grad, const float *loss,
+                                const float *flags, float *out, void *stream) {
+    const char *fn = "gsv_halo_accumulate";
+    gsv::HaloPeers P;
+    long long total;
+    int32_t dummy_slots[gsv::kHaloMaxRanks] = {0};
+    GSV_REQUIRE(n >= 0 && C >= 1 && C <= 4 &&
+                    make_peers(world, rank, nullptr, seg_off, dummy_slots, P, total),
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
+    GSV_REQUIRE(recv && loss && flags && out &&
+                    (n == 0 || (slot_map && pos3d_radii_grad && conics_grad &&
+                                intensities_grad)),
+                GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    return cuda_status(gsv::launch_halo_accumulate(
+                           n, C, P, slot_map, recv, pos3d_radii_grad,
+                           conics_grad, intensities_grad, loss, flags, out,
+                           as_stream(stream)),
                        fn);
 }
 

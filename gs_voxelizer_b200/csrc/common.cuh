@@ -72,6 +72,20 @@ enum ProfKind { kProfForward = 0, kProfBackwardGauss = 1, kProfBackwardVoxel = 2
 void profile_mark(int kind, bool stop, cudaStream_t stream);
 
 // 2^x on the special-function unit (MUFU.EX2), flush-to-zero.
+// Halo exchange of owner-sharded Gaussians (halo.cu): record sizes in
+// floats and the per-call description of the peers, passed to the kernels
+// by value.
+constexpr int kHaloMaxRanks = 64;
+constexpr int kHaloRec = 20;   // render record: pr 4, conic 6, I 4, tile box 6
+constexpr int kHaloGrad = 16;  // gradient record: pr 4, conic 6, I 4, pad 2
+struct HaloPeers {
+    int world, rank;
+    int tz0[kHaloMaxRanks], tz1[kHaloMaxRanks];  // tile-z range of each slab
+    long long off[kHaloMaxRanks];                // segment start (records)
+    int cap[kHaloMaxRanks];                      // slots per segment
+    long long loff[kHaloMaxRanks];               // local index of slot 0 - n_own
+};
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

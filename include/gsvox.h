@@ -320,6 +320,74 @@ GSV_API int gsv_voxelize_forward_noalloc(
     const float *pos3d_radii, const float *conics, const float *intensities,
     float *out_vol, void *stream);
 
+/*
+ * Halo exchange for owner-sharded z-slabs (one process per GPU). No
+ * reference counterpart: the reference is single-GPU. Every rank owns a
+ * subset of the Gaussians and projects only those; an owned Gaussian whose
+ * tile box reaches another rank's slab is sent there as a render record of
+ * GSV_HALO_RECORD_FLOATS floats (pos3d_radii 4, conic 6, intensities 4,
+ * tile_min/tile_max 6 as int bits), and the gradients of those records
+ * (GSV_HALO_GRAD_FLOATS floats: pos3d_radii 4, conic 6, intensities 4, pad)
+ * come back to the owner. A buffer holds one segment per peer rank: a
+ * header record, then seg_slots[peer] record slots, starting at record
+ * seg_off[peer] (the rank's own entry is ignored). The caller moves the
+ * buffers between ranks (an all-to-all); slab_tz is [world][2] tile-z ranges
+ * [begin, end) of every rank's slab; all per-peer arrays are host memory,
+ * world <= 64.
+ *
+ * gsv_halo_pack: records of the n owned Gaussians into `send` (slots in
+ * owner-index order, so deterministic; Gaussians past a segment's slots are
+ * dropped and flagged in its header) and slot_map[n][world] = slot or -1;
+ * counts_out (nullable, device int64[world]) = the unclamped number of
+ * Gaussians for every peer (0 for the rank itself), for sizing segments.
+ * gsv_halo_unpack: the received records into the local arrays at
+ * n_own + (slots of the lower-ranked peers) + slot, unused slots as
+ * Gaussians with an empty tile box; flags[1] = 1 if a sender overflowed.
+ * gsv_halo_pack_grads: gradients of those local entries back into the
+ * owners' segments (same slots), header = (loss[0], max(flags[0..1])).
+ * gsv_halo_accumulate: the owner adds the received gradients to its n owned
+ * entries in rank order; out[0] = sum of all ranks' losses in rank order,
+ * out[1] = max of all ranks' flags.
+ */
+#define GSV_HALO_RECORD_FLOATS 20
+#define GSV_HALO_GRAD_FLOATS 16
+
+GSV_API size_t gsv_halo_workspace_bytes(int32_t num_gaussians, int32_t world);
+
+GSV_API int gsv_halo_pack(int32_t num_gaussians, int32_t channels,
+                          const float *pos3d_radii, const float *conics,
+                          const float *intensities, const int32_t *tile_min,
+                          const int32_t *tile_max, int32_t world, int32_t rank,
+                          const int32_t *slab_tz, const int64_t *seg_off,
+                          const int32_t *seg_slots, float *send,
+                          int32_t *slot_map, int64_t *counts_out,
+                          void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+GSV_API int gsv_halo_unpack(int32_t n_own, int32_t channels, int32_t world,
+                            int32_t rank, const int64_t *seg_off,
+                            const int32_t *seg_slots, const float *recv,
+                            float *pos3d_radii, float *conics,
+                            float *intensities, int32_t *tile_min,
+                            int32_t *tile_max, float *flags, void *stream);
+
+GSV_API int gsv_halo_pack_grads(int32_t n_own, int32_t channels, int32_t world,
+                                int32_t rank, const int64_t *seg_off,
+                                const int32_t *seg_slots,
+                                const float *pos3d_radii_grad,
+                                const float *conics_grad,
+                                const float *intensities_grad,
+                                const float *loss, const float *flags,
+                                float *send, void *stream);
+
+GSV_API int gsv_halo_accumulate(int32_t num_gaussians, int32_t channels,
+                                int32_t world, int32_t rank,
+                                const int64_t *seg_off, const int32_t *slot_map,
+                                const float *recv, float *pos3d_radii_grad,
+                                float *conics_grad, float *intensities_grad,
+                                const float *loss, const float *flags,
+                                float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

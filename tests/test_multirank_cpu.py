@@ -128,3 +128,22 @@ def test_rank_failure_surfaces_as_error(tmp_path):
             p.kill()
     assert os.path.exists(out)
     assert open(out).read().startswith("error:")
+
+
+def test_owner_of_assigns_each_centre_to_its_slab():
+    """halo.owner_of: the rank whose z-slab holds each Gaussian's centre,
+    consistent with slab_bounds; centres outside the volume go to the
+    nearest slab."""
+    from gs_voxelizer_b200.halo import owner_of
+    from gs_voxelizer_b200.slab import slab_bounds
+    vol, world_size, center = (100, 30, 20), (2.0, 1.0, 1.0), (1.0, 0.5, 0.5)
+    rng = np.random.default_rng(0)
+    pos = rng.uniform(-0.2, 2.2, size=(5000, 3)).astype(np.float32)
+    for world in (1, 2, 3, 5):
+        own = owner_of(pos, vol, world_size, center, world)
+        assert own.min() >= 0 and own.max() < world
+        zv = pos[:, 2].astype(np.float64) / 2.0 * 100  # volume starts at z = 0
+        tile = np.clip(np.floor(zv / 8), 0, 12)
+        for r in range(world):
+            tz0, tz1 = slab_bounds(vol, world, r)
+            assert ((tile >= tz0) & (tile < tz1) == (own == r)).all()

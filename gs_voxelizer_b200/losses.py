@@ -74,7 +74,7 @@ def l1_loss(vol: torch.Tensor, target: torch.Tensor,
 class _VoxelizeL1(Function):
     @staticmethod
     def forward(ctx, pos3d_radii, conics, intensities, target, plan,
-                tile_min, tile_max, denom, group):
+                tile_min, tile_max, denom, group, reduce):
         one_d = intensities.dim() == 1
         if one_d:
             intensities = intensities.unsqueeze(-1)
@@ -106,6 +106,7 @@ class _VoxelizeL1(Function):
             _C._stream(dev)))
         ctx.ws = ws
         ctx.plan, ctx.denom, ctx.group, ctx.one_d = plan, float(denom), group, one_d
+        ctx.reduce = reduce
         ctx.save_for_backward(pos3d_radii, conics, intensities, ids, bins, out,
                               target)
         ctx.mark_non_differentiable(out)
@@ -131,10 +132,11 @@ class _VoxelizeL1(Function):
             _C._ptr(out), _C._ptr(target), grad_loss.data_ptr(), ctx.denom,
             _C._ptr(gp), _C._ptr(gc), _C._ptr(gi), ws.data_ptr(), ws.numel(),
             _C._stream(dev)))
-        gp, gc, gi = allreduce_gaussian_grads([gp, gc, gi], ctx.group)
+        if ctx.reduce:
+            gp, gc, gi = allreduce_gaussian_grads([gp, gc, gi], ctx.group)
         if ctx.one_d:
             gi = gi.reshape(-1)
-        return gp, gc, gi, None, None, None, None, None, None
+        return gp, gc, gi, None, None, None, None, None, None, None
 
 
 def voxelize_gaussians_l1(
@@ -154,12 +156,15 @@ def voxelize_gaussians_l1(
     Args: as ``voxelize.voxelize_gaussians`` plus
         target: [Z,Y,X,C] float32 target (the slab's part with a plan).
         denom: normaliser; default the full volume's element count (mean).
-        plan: SlabPlan for z-slab sharding; default the whole volume.
-        group: process group for the gradient all-reduce (slab mode).
+        plan: SlabPlan for z-slab sharding; default the whole volume (then no
+            collective, even inside a distributed job).
+        group: process group for the gradient all-reduce (slab mode; default
+            the default group when torch.distributed is initialised).
     Returns:
         (loss, volume): loss is a 0-d tensor (this slab's share with a plan),
         volume the forward volume (no gradient).
     """
+    reduce = plan is not None
     if plan is None:
         plan = SlabPlan(vol_size_voxel, 0, tile_layers(vol_size_voxel))
     if denom is None:
@@ -169,4 +174,4 @@ def voxelize_gaussians_l1(
     return _VoxelizeL1.apply(pos3d_radii.contiguous(), conics.contiguous(),
                              intensities.contiguous(), target.contiguous(),
                              plan, tile_min.contiguous(),
-                             tile_max.contiguous(), denom, group)
+                             tile_max.contiguous(), denom, group, reduce)

@@ -53,8 +53,9 @@ class FusedL1Step:
             ``optim_to_render``.
         target: [Z,Y,X,C] float32 target of this rank's slab.
         denom: loss normaliser (default: element count of the full volume).
-        plan: z-slab of this rank (default: the whole volume).
-        group: process group whose ranks hold the other slabs.
+        plan: z-slab of this rank (default: the whole volume, no collective).
+        group: process group whose ranks hold the other slabs (with a plan;
+            default: the default group when torch.distributed is initialised).
         headroom: capacity of the pair buffer relative to the last count.
         use_graph: capture and replay CUDA graphs (False: launch eagerly).
     """
@@ -99,8 +100,11 @@ class FusedL1Step:
             raise ValueError("denom must be non-zero")
         self.denom = float(denom)
         self.group = group
+        # only slabs are summed over ranks: a step over the whole volume is
+        # complete on its own, even inside a distributed job
         self.ranks = (dist.get_world_size(group)
-                      if dist.is_available() and dist.is_initialized() else 1)
+                      if plan is not None and dist.is_available()
+                      and dist.is_initialized() else 1)
         if headroom < 1.0:
             raise ValueError("headroom must be >= 1")
         self.headroom = float(headroom)

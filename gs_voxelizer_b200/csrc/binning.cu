@@ -49,13 +49,16 @@ enum ExpandMode { kCount = 0, kScatter = 1 };
 
 // mode kCount:   counts[tile] += 1 for every pair
 // mode kScatter: ids[cursor[tile]++] = gaussian for every pair
+// Gaussians are taken in the order `order` gives (all n of them), or in
+// index order when it is null.
 template <int MODE>
 __global__ void __launch_bounds__(256)
 expand_pairs_kernel(int n, const int *__restrict__ tmin,
                     const int *__restrict__ tmax, int Tx, int Ty, int tz0,
                     int tz1, int *__restrict__ counter,
                     int *__restrict__ ids_out, long long capacity,
-                    int *__restrict__ error_flag) {
+                    int *__restrict__ error_flag,
+                    const int *__restrict__ order) {
     const int lane = threadIdx.x & 31;
     const long long warp_global =
         ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -63,7 +66,11 @@ expand_pairs_kernel(int n, const int *__restrict__ tmin,
     for (long long w = warp_global; w * 32 < n; w += warps_total) {
         const long long gi = w * 32 + lane;
         Box b = {0, 0, 0, 0, 0, 0};
-        if (gi < n) b = load_box(tmin, tmax, (int)gi, tz0, tz1);
+        int gid = 0;
+        if (gi < n) {
+            gid = order ? order[gi] : (int)gi;
+            b = load_box(tmin, tmax, gid, tz0, tz1);
+        }
         const int cnt = b.nx * b.ny * b.nz;
         const int incl = warp_inclusive_scan(cnt);
         const int excl = incl - cnt;
@@ -85,6 +92,7 @@ expand_pairs_kernel(int n, const int *__restrict__ tmin,
             const int o_z0 = __shfl_sync(0xffffffffu, b.z0, owner);
             const int o_nx = __shfl_sync(0xffffffffu, b.nx, owner);
             const int o_ny = __shfl_sync(0xffffffffu, b.ny, owner);
+            const int o_gid = __shfl_sync(0xffffffffu, gid, owner);
             if (k < total) {
                 int r = k - o_excl;
                 const int x = r % o_nx;
@@ -98,7 +106,7 @@ expand_pairs_kernel(int n, const int *__restrict__ tmin,
                 } else {
                     const int slot = atomicAdd(counter + tile, 1);
                     if (slot >= 0 && slot < capacity) {
-                        ids_out[slot] = (int)(w * 32 + owner);
+                        ids_out[slot] = o_gid;
                     } else {
                         *error_flag = 1;
                     }
@@ -148,6 +156,75 @@ __device__ __forceinline__ long long block_excl_scan_ll(long long v,
     *total = smem[nw - 1];
     __syncthreads();
     return warp_prefix + incl - v;
+}
+
+// ---- processing order by tile layer --------------------------------------
+//
+// With hundreds of millions of pairs the id array (4 B per pair) is far
+// larger than L2, and the scatter's writes, random over that array, become
+// DRAM read-modify-writes. Taking the Gaussians grouped by the (slab-
+// relative) tile layer of their box's lower z corner keeps the warps in
+// flight on a band of adjacent layers, whose segments stay in L2. The order
+// is a counting sort of the Gaussians (not of the pairs) into one bucket
+// per layer, plus a last bucket for Gaussians with no tile in the slab. Ids
+// within a tile are sorted afterwards either way, so results do not change.
+
+constexpr long long kOrderMinPairs = 1LL << 25;
+
+__device__ __forceinline__ int layer_bucket(const int *tmin, const int *tmax,
+                                            int i, int tz0, int tz1) {
+    const Box b = load_box(tmin, tmax, i, tz0, tz1);
+    return (b.nx > 0 && b.ny > 0 && b.nz > 0) ? b.z0 - tz0 : tz1 - tz0;
+}
+
+__global__ void __launch_bounds__(256)
+layer_count_kernel(int n, const int *__restrict__ tmin,
+                   const int *__restrict__ tmax, int tz0, int tz1,
+                   int *__restrict__ counts) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned active = __ballot_sync(0xffffffffu, i < n);
+    if (i >= n) return;
+    const int key = layer_bucket(tmin, tmax, i, tz0, tz1);
+    const unsigned peers = __match_any_sync(active, key);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1)
+        atomicAdd(&counts[key], __popc(peers));
+}
+
+// single CTA: counts -> exclusive offsets (the scatter's cursors), in place
+__global__ void __launch_bounds__(1024)
+layer_scan_kernel(int nb, int *__restrict__ counts) {
+    __shared__ long long smem[32];
+    const int per = (nb + 1023) / 1024;
+    const int begin = threadIdx.x * per;
+    long long local = 0;
+    for (int k = 0; k < per; ++k)
+        if (begin + k < nb) local += counts[begin + k];
+    long long total;
+    long long run = block_excl_scan_ll(local, smem, &total);
+    for (int k = 0; k < per; ++k) {
+        if (begin + k < nb) {
+            const int v = counts[begin + k];
+            counts[begin + k] = (int)run;
+            run += v;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+layer_scatter_kernel(int n, const int *__restrict__ tmin,
+                     const int *__restrict__ tmax, int tz0, int tz1,
+                     int *__restrict__ cursor, int *__restrict__ order) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const unsigned active = __ballot_sync(0xffffffffu, i < n);
+    if (i >= n) return;
+    const int key = layer_bucket(tmin, tmax, i, tz0, tz1);
+    const unsigned peers = __match_any_sync(active, key);
+    const int leader = __ffs(peers) - 1;
+    int base = 0;
+    if (lane == leader) base = atomicAdd(&cursor[key], __popc(peers));
+    base = __shfl_sync(active, base, leader);
+    order[base + __popc(peers & ((1u << lane) - 1u))] = i;
 }
 
 // Work items of the per-Gaussian backward for a tile of c pairs.
@@ -477,12 +554,18 @@ sort_segments_cta_kernel(const int2 *__restrict__ tile_bins,
 //   big_list[T]  int, big_count int, error flag int
 //   tmp     [I]  int  (radix temporary for huge segments)
 struct BinLayout {
-    size_t counts, partials, big_list, flags, tmp, total;
+    size_t counts, partials, big_list, flags, tmp, layer, order, total;
+    bool ordered;  // Gaussians taken in tile-layer order (large pair counts)
 };
 
 static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-BinLayout bin_layout(long long ntiles, long long nisect) {
+static bool use_layer_order(long long nisect, long long layers) {
+    return nisect >= kOrderMinPairs && layers > 1;
+}
+
+BinLayout bin_layout(long long ntiles, long long nisect, long long n,
+                     long long layers) {
     BinLayout L;
     const long long nblocks = (ntiles + kScanTile - 1) / kScanTile;
     size_t off = 0;
@@ -496,12 +579,18 @@ BinLayout bin_layout(long long ntiles, long long nisect) {
     off = align256(off + sizeof(int) * 4);
     L.tmp = off;
     off = align256(off + sizeof(int) * (size_t)nisect);
+    L.ordered = use_layer_order(nisect, layers);
+    L.layer = off;
+    if (L.ordered) off = align256(off + sizeof(int) * (size_t)(layers + 1));
+    L.order = off;
+    if (L.ordered) off = align256(off + sizeof(int) * (size_t)(n > 0 ? n : 1));
     L.total = off;
     return L;
 }
 
-size_t bin_workspace_bytes(long long ntiles, long long nisect) {
-    return bin_layout(ntiles, nisect).total;
+size_t bin_workspace_bytes(long long ntiles, long long nisect, long long n,
+                           long long layers) {
+    return bin_layout(ntiles, nisect, n, layers).total;
 }
 
 long long scan_blocks(long long ntiles) {
@@ -540,7 +629,7 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
                            cudaStream_t stream, long long *count_out,
                            float *overflow_out, const ItemScan *items) {
     const long long ntiles = (long long)(tz1 - tz0) * Ty * Tx;
-    const BinLayout L = bin_layout(ntiles, nisect);
+    const BinLayout L = bin_layout(ntiles, nisect, n, tz1 - tz0);
     char *base = static_cast<char *>(ws);
     int *counts = reinterpret_cast<int *>(base + L.counts);
     long long *partials = reinterpret_cast<long long *>(base + L.partials);
@@ -561,11 +650,28 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
             return err;
         return cudaSuccess;
     }
+    const int *order = nullptr;
+    if (L.ordered && n > 0 && nisect > 0) {
+        int *layer = reinterpret_cast<int *>(base + L.layer);
+        int *ord = reinterpret_cast<int *>(base + L.order);
+        const int nb = tz1 - tz0 + 1;
+        if ((err = cudaMemsetAsync(layer, 0, sizeof(int) * nb, stream)))
+            return err;
+        const unsigned gb = (unsigned)((n + 255) / 256);
+        layer_count_kernel<<<gb, 256, 0, stream>>>(n, tmin, tmax, tz0, tz1,
+                                                   layer);
+        layer_scan_kernel<<<1, 1024, 0, stream>>>(nb, layer);
+        layer_scatter_kernel<<<gb, 256, 0, stream>>>(n, tmin, tmax, tz0, tz1,
+                                                     layer, ord);
+        count_launches(3);
+        order = ord;
+    }
     if (n > 0 && (nisect > 0 || count_out || overflow_out)) {
         const int warps = (n + 31) / 32;
         const int blocks = min((warps + 7) / 8, kSMs * 16);
         expand_pairs_kernel<kCount><<<blocks, 256, 0, stream>>>(
-            n, tmin, tmax, Tx, Ty, tz0, tz1, counts, nullptr, 0, flags + 1);
+            n, tmin, tmax, Tx, Ty, tz0, tz1, counts, nullptr, 0, flags + 1,
+            order);
         count_launches(1);
     }
     if ((err = scan_counts_to_bins(counts, ntiles, partials, tile_bins, stream,
@@ -577,7 +683,7 @@ cudaError_t launch_binning(int n, long long nisect, const int *tmin,
         const int blocks = min((warps + 7) / 8, kSMs * 16);
         expand_pairs_kernel<kScatter><<<blocks, 256, 0, stream>>>(
             n, tmin, tmax, Tx, Ty, tz0, tz1, counts, ids_out, nisect,
-            flags + 1);
+            flags + 1, order);
     }
     {
         const long long warps_needed = ntiles;

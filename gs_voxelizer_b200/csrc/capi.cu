@@ -24,7 +24,8 @@ cudaError_t launch_project_bwd(int n, const float *pos3d, const float *scale3d,
                                const float *conics_grad, const float *pos_radii,
                                float *pos_grad, float *scale_grad,
                                float *quat_grad, cudaStream_t stream);
-size_t bin_workspace_bytes(long long ntiles, long long nisect);
+size_t bin_workspace_bytes(long long ntiles, long long nisect, long long n,
+                           long long layers);
 cudaError_t launch_binning(int n, long long nisect, const int *tmin,
                            const int *tmax, int Tx, int Ty, int tz0, int tz1,
                            int *ids_out, int *tile_bins, void *ws,
@@ -191,7 +192,8 @@ int binning_impl(const char *fn, int32_t n, int64_t nisect,
                 "%s: tile_bins is null", fn);
     GSV_REQUIRE(nisect == 0 || (ids_out && tile_min && tile_max),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null input/output pointer", fn);
-    const size_t need = gsv::bin_workspace_bytes(ntiles, nisect);
+    const size_t need =
+        gsv::bin_workspace_bytes(ntiles, nisect, n, g.slab_tiles_z());
     GSV_REQUIRE(ws_bytes >= need && (need == 0 || ws),
                 GSV_ERR_WORKSPACE_TOO_SMALL,
                 "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes,
@@ -280,8 +282,9 @@ int backward_impl(const char *fn, bool per_gaussian, const gsv::Geom &g,
 }
 
 // Binning part of the fused-L1 workspace (256-byte aligned).
-size_t l1_bin_part(const gsv::Geom &g, long long nisect) {
-    return (gsv::bin_workspace_bytes(g.slab_tiles(), nisect) + 255) &
+size_t l1_bin_part(const gsv::Geom &g, long long nisect, long long n) {
+    return (gsv::bin_workspace_bytes(g.slab_tiles(), nisect, n,
+                                     g.slab_tiles_z()) + 255) &
            ~size_t(255);
 }
 
@@ -380,10 +383,10 @@ int gsv_optim_to_render_backward(int32_t n, const float *pos3d,
 
 size_t gsv_bin_and_sort_workspace_bytes(int32_t n, int64_t nisect,
                                         const int32_t vol[3]) {
-    (void)n;
     if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
     const gsv::Geom g = gsv::make_geom(vol);
-    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect);
+    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect,
+                                    n < 0 ? 0 : n, g.slab_tiles_z());
 }
 
 int gsv_bin_and_sort_gaussians(int32_t n, int64_t nisect,
@@ -404,11 +407,11 @@ int gsv_bin_and_sort_gaussians(int32_t n, int64_t nisect,
 size_t gsv_bin_and_sort_slab_workspace_bytes(int32_t n, int64_t nisect,
                                              const int32_t vol[3],
                                              int32_t tz0, int32_t tz1) {
-    (void)n;
     if (!vol || vol[0] <= 0 || vol[1] <= 0 || vol[2] <= 0) return 0;
     const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
     if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
-    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect);
+    return gsv::bin_workspace_bytes(g.slab_tiles(), nisect < 0 ? 0 : nisect,
+                                    n < 0 ? 0 : n, g.slab_tiles_z());
 }
 
 int gsv_bin_and_sort_gaussians_slab(int32_t n, int64_t nisect,
@@ -566,7 +569,7 @@ size_t gsv_voxelize_l1_workspace_bytes(int32_t n, int32_t C, int64_t nisect,
     const gsv::Geom g = gsv::make_geom(vol, tz0, tz1);
     if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
     const long long ni = nisect < 0 ? 0 : nisect;
-    return l1_bin_part(g, ni) +
+    return l1_bin_part(g, ni, n < 0 ? 0 : n) +
            gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(), ni);
 }
 
@@ -607,7 +610,7 @@ int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
                 GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
     cudaStream_t s = as_stream(stream);
     char *bin_ws = static_cast<char *>(ws);
-    char *vox_ws = bin_ws + l1_bin_part(g, nisect);
+    char *vox_ws = bin_ws + l1_bin_part(g, nisect, n);
     gsv::enable_large_smem();
     // the binning also scans and writes the backward's work plan
     const gsv::ItemScan items =
@@ -658,7 +661,7 @@ int gsv_voxelize_backward_per_gaussian_l1(
                                 target && grad_loss),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
     GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
-    char *vox_ws = static_cast<char *>(ws) + l1_bin_part(g, nisect);
+    char *vox_ws = static_cast<char *>(ws) + l1_bin_part(g, nisect, n);
     return cuda_status(gsv::launch_vox_backward_gauss(
                            g, C, n, nisect, ids, bins, pos, con, inten,
                            out_vol, pos_grad, con_grad, int_grad, vox_ws,

@@ -14,7 +14,17 @@
 //     cull rewritten as a threshold on the log2 exponent (s >= thr).
 //   * sigma along a line of 8 voxels in z is a quadratic P + L*dz + C*dz^2;
 //     P and L are formed once per (Gaussian, column), so an evaluation costs
-//     two FMAs, a compare and one ex2.
+//     two FMAs and one ex2 - executed as paired FP32 instructions
+//     (FFMA2/FMUL2/FADD2), two evaluations per instruction.
+//   * The cull costs no compare for robustly positive-definite Gaussians
+//     with -126 <= thr <= -1: the forward multiplies alpha by 2^(-thr-126)
+//     with a flush-to-zero multiply (exactly 0 below the threshold) and
+//     accumulates with I * 2^(thr+126); the backward evaluates
+//     ex2(s - thr - 126), flushed to 0 by ex2.approx.ftz, on a dL/dvol tile
+//     staged x 2^K and rescales each Gaussian's sums once. Other Gaussians
+//     take the exact compare path.
+//   * Forward: exponentials by recurrence along z (two ex2 anchors per
+//     column of 8) where the anchor provably never underflows.
 //   * "sigma > 0" can only happen for a conic that is not positive definite
 //     or is so ill-conditioned that rounding flips the sign. The record marks
 //     Gaussians whose conic satisfies det(Q) >= 1e-5 trace(Q)^3 (so

@@ -17,7 +17,7 @@ accessed out of bounds) and the results are invalid, so ``run()`` grows the
 buffers and runs the step again before returning; growth is rare (the
 capacity keeps 25 % headroom). Because the launch sequence and every
 address are fixed, the whole step is captured once as a CUDA graph and
-replayed: one graph launch per step instead of ~25 kernel launches and the
+replayed: one graph launch per step instead of 14 kernel launches and the
 Python around them.
 
 With a process group of more than one rank (z-slab sharding), the step is

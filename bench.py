@@ -511,6 +511,7 @@ def main():
                          "the reference's voxel index is int32 (voxelize.cu:63); "
                          "a 2048^3 volume overflows it"}))
         return
+    ref_world = world  # the reference runs the N-GPU arm's workload on one GPU
     if impl == "reference":
         world = 1
         from oracle import ref_api
@@ -524,12 +525,13 @@ def main():
         from gs_voxelizer_b200.workloads import CONFIGS
         cfg = CONFIGS["shard2048"]
     else:
-        cfg = workload(world)
+        cfg = workload(ref_world if impl == "reference" else world)
     if args.small:
         from gs_voxelizer_b200.workloads import Config
         cfg = Config("small128", (128, 128, 128), 25_000, pos=cfg.pos,
                      scale=(0.004, 0.04), intensity=cfg.intensity, ellipsoids=16)
-    inputs = make_inputs(cfg, 1 if strong else world)
+    inputs = make_inputs(cfg, 1 if strong else
+                         (ref_world if impl == "reference" else world))
     st = Step(impl, cfg, world, rank, inputs)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     if args.profile_run:
@@ -640,6 +642,9 @@ def main():
         out["impl"] = "reference"
         out["reference_build"] = ("reference CUDA sources compiled for sm_100a "
                                   "(oracle/build_ref.py), run on the same GPU")
+        if ref_world > 1:
+            out["reference_note"] = (f"single-GPU reference on the workload of the "
+                                     f"{ref_world}-GPU arm ({cfg.name})")
         out["gpu_launches"] = None
     else:
         out["impl"] = "ours"
@@ -667,9 +672,11 @@ def main():
             out["cpu_baseline"] = {"error": str(exc)}
     if rank == 0:
         emit(json.dumps(out))
-    if world > 1:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    finally:
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()

@@ -117,6 +117,32 @@ def test_projection_backward_parity():
         assert_grad_close(host(got), want, name)
 
 
+def test_pos3d_radii_buffer():
+    """optim_to_render(..., pos3d_radii_buffer=buf) returns buf itself, filled
+    with the projection, gradients flow through it, and a wrong buffer
+    raises ValueError (gs_voxelizer/optim_to_render.py:98-113)."""
+    from gs_voxelizer_b200.optim_to_render import optim_to_render
+    cfg = K.small_config(vol=(24, 32, 40), n=500, seed=23)
+    arrs = K.inputs(cfg)
+    leaves = [dev(a).requires_grad_(True) for a in arrs]
+    a = optim_to_render(*leaves, cfg.vol, cfg.world, cfg.center)
+    buf = torch.empty((cfg.n, 4), device="cuda")
+    leaves2 = [dev(x).requires_grad_(True) for x in arrs]
+    b = optim_to_render(*leaves2, cfg.vol, cfg.world, cfg.center,
+                        pos3d_radii_buffer=buf)
+    assert b[0].data_ptr() == buf.data_ptr()
+    assert torch.equal(a[0], b[0])
+    (a[0].sum() + a[1].sum()).backward()
+    (b[0].sum() + b[1].sum()).backward()
+    for x, y in zip(leaves[:3], leaves2[:3]):
+        assert torch.equal(x.grad, y.grad)
+    for bad in (torch.empty((cfg.n, 3), device="cuda"),
+                torch.empty((cfg.n, 4), device="cuda", dtype=torch.float64)):
+        with pytest.raises(ValueError):
+            optim_to_render(*leaves, cfg.vol, cfg.world, cfg.center,
+                            pos3d_radii_buffer=bad)
+
+
 # ---------------------------------------------------------------- binning
 
 @pytest.mark.parametrize("vol,n,scale", [

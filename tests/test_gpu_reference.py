@@ -47,6 +47,10 @@ CASES = [
     dict(vol=(60, 50, 70), n=3000, channels=1, scale=(0.005, 0.05)),
     dict(vol=(33, 40, 27), n=1500, channels=3, scale=(0.005, 0.06)),
     dict(vol=(64, 64, 64), n=8000, channels=4, scale=(0.002, 0.03)),
+    # the reference's multi-channel test setting: 2 channels, non-unit world
+    # size, volume off the origin
+    dict(vol=(48, 36, 60), n=3000, channels=2, scale=(0.005, 0.05),
+         pos=(0.0, 1.4), world=(1.2, 0.9, 1.5), center=(0.7, 0.35, 0.8)),
 ]
 
 

@@ -16,6 +16,20 @@ Metric: Gaussian-voxel evaluations per second over the whole step, counting
 each (Gaussian, voxel) pair once in the forward and once in the backward
 pass (E from the binning: sum over tiles of Gaussians x voxels).
 
+The JSON line: `value` / `ms_per_step` time the sync-free step
+(step.FusedL1Step, halo.HaloL1Step at N > 1) replayed as CUDA graphs with
+inputs resident on the device; `e2e` the same step through its public call
+with the parameters copied from pinned host memory and the loss read back
+each step; `autograd` and `dropin` the same step through
+losses.voxelize_gaussians_l1 and through the reference-compatible API +
+torch L1; `fwd_ms` / `bwd_ms` split the autograd step; `roofline` the
+dominant kernel (CUDA events recorded by the library around it) against
+the MUFU bound, with the DRAM traffic of the committed ncu summary;
+`cpu_baseline` the C oracle on the host cores (N = 1); `clocks` nvidia-smi
+samples taken during the timed region. `--impl reference` runs the
+reference's own extension (built from its sources by oracle/build_ref.py)
+on the same workload.
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N
 """

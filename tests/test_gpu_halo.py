@@ -184,3 +184,25 @@ def test_halo_single_rank_graph():
     assert torch.equal(step.volume, want_vol)
     for p, g, name in zip(params, want_grads, ("pos3d", "scale3d", "quat", "intensity")):
         close(p.grad, g, 1e-4, 1e-4, name)
+
+
+def test_halo_ranks_without_gaussians():
+    """All Gaussians in the lowest slab of three: ranks 1 and 2 own none
+    (rank 1 still receives rank 0's boundary Gaussians)."""
+    from gs_voxelizer_b200.halo import owner_of
+    from gs_voxelizer_b200.workloads import phantom
+    cfg = K.small_config(vol=(72, 40, 48), n=2000, seed=83, pos=(0.0, 0.3),
+                         scale=(0.01, 0.05))
+    arrs = list(K.inputs(cfg))
+    owners = owner_of(arrs[0], cfg.vol, cfg.world, cfg.center, 3)
+    assert (owners == 2).sum() == 0
+    target = phantom(cfg, device="cuda")
+    want_loss, want_grads, _ = _reference(cfg, arrs, target)
+    res = _run_ranks(cfg, 3, arrs, target, steps=1)
+    for r in res:
+        assert r["losses"][0] == pytest.approx(want_loss, rel=1e-5)
+    assert res[2]["step"].n == 0
+    got = torch.zeros_like(want_grads[0])
+    for r in res:
+        got[torch.from_numpy(r["idx"]).cuda()] = r["grads"][0]
+    close(got, want_grads[0], 1e-4, 1e-4, "pos3d")

@@ -154,3 +154,25 @@ def test_step_many_tiles(force_overflow):
     assert int(step.count.item()) <= step.capacity
     assert loss == pytest.approx(want[0], rel=1e-5)
     _compare(step, params, want)
+
+
+@pytest.mark.parametrize("vol,channels,tz", [((19, 23, 29), 3, None),
+                                             ((43, 17, 21), 1, (2, 6)),
+                                             ((9, 8, 7), 4, None)])
+def test_step_odd_shapes(vol, channels, tz):
+    """Dimensions that are not multiples of 8 (or of 4): the fused loss's
+    unaligned staging and epilogue paths; a slab ending in a partial tile
+    layer."""
+    from gs_voxelizer_b200.slab import SlabPlan
+    from gs_voxelizer_b200.workloads import phantom
+    cfg = K.small_config(vol=vol, n=1500, seed=75, channels=channels,
+                         scale=(0.01, 0.08))
+    plan = SlabPlan(cfg.vol, *tz) if tz else None
+    zr = (plan.z_begin, plan.z_end) if plan else None
+    target = phantom(cfg, device="cuda", z_range=zr)
+    want = _autograd(cfg, target, plan=plan)
+    params, step = _step(cfg, target, plan=plan)
+    for _ in range(2):
+        loss = step.run()
+        assert loss == pytest.approx(want[0], rel=1e-5)
+        _compare(step, params, want)

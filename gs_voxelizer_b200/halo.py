@@ -79,6 +79,20 @@ class NcclComm:
                                group=self.group)
 
 
+def segments(slots: Sequence[int], rank: int, rec: int) -> Tuple[List[int], List[int], int]:
+    """Layout of an exchange buffer with one segment per peer: a header
+    record plus slots[peer] record slots (none for the rank itself). Returns
+    the element count of every segment (the all-to-all split sizes), the
+    record offset of every segment and the total number of records."""
+    counts, offs, off = [], [], 0
+    for d, k in enumerate(slots):
+        k = 0 if d == rank else int(k) + 1
+        offs.append(off)
+        counts.append(k * rec)
+        off += k
+    return counts, offs, off
+
+
 def _i64(vals) -> ctypes.Array:
     return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
 
@@ -175,7 +189,7 @@ class HaloL1Step:
     def _alloc_local(self) -> None:
         """Local arrays: owned Gaussians first, then the halo slots of every
         peer in rank order; send / receive buffers of both exchanges."""
-        n, C, dev, W = self.n, self.C, self.device, self.world
+        n, C, dev = self.n, self.C, self.device
         self.n_loc = n + sum(self.caps_in)
         f32 = dict(dtype=torch.float32, device=dev)
         i32 = dict(dtype=torch.int32, device=dev)
@@ -190,19 +204,10 @@ class HaloL1Step:
         self.gc = torch.zeros((L, 6), **f32)
         self.gi = torch.zeros((L, C), **f32)
 
-        def segs(slots, rec):
-            counts, offs, off = [], [], 0
-            for d in range(W):
-                k = 0 if d == self.rank else slots[d] + 1
-                offs.append(off)
-                counts.append(k * rec)
-                off += k
-            return counts, offs, off
-
-        self.c1_send, self.o1_send, r1s = segs(self.caps_out, REC)
-        self.c1_recv, self.o1_recv, r1r = segs(self.caps_in, REC)
-        self.c2_send, self.o2_send, r2s = segs(self.caps_in, GREC)
-        self.c2_recv, self.o2_recv, r2r = segs(self.caps_out, GREC)
+        self.c1_send, self.o1_send, r1s = segments(self.caps_out, self.rank, REC)
+        self.c1_recv, self.o1_recv, r1r = segments(self.caps_in, self.rank, REC)
+        self.c2_send, self.o2_send, r2s = segments(self.caps_in, self.rank, GREC)
+        self.c2_recv, self.o2_recv, r2r = segments(self.caps_out, self.rank, GREC)
         self.send1 = torch.zeros((max(r1s, 1) * REC,), **f32)
         self.recv1 = torch.zeros((max(r1r, 1) * REC,), **f32)
         self.send2 = torch.zeros((max(r2s, 1) * GREC,), **f32)

@@ -147,3 +147,42 @@ def test_owner_of_assigns_each_centre_to_its_slab():
         for r in range(world):
             tz0, tz1 = slab_bounds(vol, world, r)
             assert ((tile >= tz0) & (tile < tz1) == (own == r)).all()
+
+
+def _halo_layout_worker(rank, world, port):
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        from gs_voxelizer_b200.halo import REC, NcclComm, segments
+        _init(rank, world, port)
+        comm = NcclComm()
+        # slots this rank sends to every peer; everyone learns the matrix
+        mine = [0 if d == rank else 3 * (rank + 1) + d for d in range(world)]
+        matrix = comm.all_gather_ints(mine, "cpu")
+        caps_out = matrix[rank]
+        caps_in = [matrix[s][rank] for s in range(world)]
+        c_send, o_send, n_send = segments(caps_out, rank, REC)
+        c_recv, o_recv, n_recv = segments(caps_in, rank, REC)
+        send = torch.full((n_send * REC,), -1.0)
+        recv = torch.full((n_recv * REC,), -2.0)
+        for d in range(world):
+            for slot in range(caps_out[d] + 1 if d != rank else 0):
+                r = (o_send[d] + slot) * REC
+                send[r:r + 3] = torch.tensor([rank, d, slot], dtype=torch.float32)
+        comm.all_to_all(send, c_send, recv, c_recv)
+        for s in range(world):
+            for slot in range(caps_in[s] + 1 if s != rank else 0):
+                r = (o_recv[s] + slot) * REC
+                assert recv[r:r + 3].tolist() == [s, rank, slot], (rank, s, slot)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        traceback.print_exc()
+        raise
+
+
+def test_halo_exchange_layout_over_gloo():
+    """halo.segments + the communicator: every rank's send segments land
+    in the peers' receive segments slot for slot (header included), with
+    capacities agreed through the all-gather (3 gloo ranks)."""
+    mp.spawn(_halo_layout_worker, args=(3, _free_port()), nprocs=3, join=True)

@@ -80,6 +80,46 @@ def test_argument_errors():
     assert lib.gsv_profile_kernel(7, None, None) == 1
 
 
+def test_halo_argument_errors():
+    """The halo entry points validate world / rank / sizes / workspace
+    before any CUDA call."""
+    from gs_voxelizer_b200._lib import lib
+    I32, I64 = ctypes.c_int32, ctypes.c_int64
+    tz = (I32 * 4)(0, 2, 2, 4)
+    off = (I64 * 2)(0, 0)
+    slots = (I32 * 2)(0, 5)
+    dummy = ctypes.c_void_p(1)
+    assert lib.gsv_halo_workspace_bytes(10, 0) == 0
+    assert lib.gsv_halo_workspace_bytes(10, 65) == 0
+    ws_need = lib.gsv_halo_workspace_bytes(10, 2)
+    assert ws_need > 0
+    # rank outside the world
+    st = lib.gsv_halo_pack(10, 1, dummy, dummy, dummy, dummy, dummy, 2, 2, tz,
+                           off, slots, dummy, dummy, None, dummy, ws_need, None)
+    assert st == 1 and b"peer description" in lib.gsv_last_error()
+    # five channels
+    st = lib.gsv_halo_pack(10, 5, dummy, dummy, dummy, dummy, dummy, 2, 0, tz,
+                           off, slots, dummy, dummy, None, dummy, ws_need, None)
+    assert st == 1
+    # workspace too small
+    st = lib.gsv_halo_pack(10, 1, dummy, dummy, dummy, dummy, dummy, 2, 0, tz,
+                           off, slots, dummy, dummy, None, dummy, ws_need - 1,
+                           None)
+    assert st == 3
+    # negative slots
+    bad = (I32 * 2)(0, -1)
+    st = lib.gsv_halo_unpack(0, 1, 2, 0, off, bad, dummy, dummy, dummy, dummy,
+                             dummy, dummy, dummy, None)
+    assert st == 1
+    # null receive buffer with slots to unpack
+    st = lib.gsv_halo_unpack(0, 1, 2, 0, off, slots, None, dummy, dummy, dummy,
+                             dummy, dummy, dummy, None)
+    assert st == 1 and b"null" in lib.gsv_last_error()
+    st = lib.gsv_halo_accumulate(3, 1, 2, 0, off, dummy, None, dummy, dummy,
+                                 dummy, dummy, dummy, dummy, None)
+    assert st == 1
+
+
 def test_python_api_rejects_cpu_tensors_like_the_reference():
     from gs_voxelizer_b200 import cuda as C
     from gs_voxelizer_b200.optim_to_render import optim_to_render

@@ -25,6 +25,10 @@ every rank re-size (one all-gather of the halo counts) and repeat the step.
 
 Gradients of the owned parameters are written to fixed tensors installed as
 their `.grad` (overwritten each step); the parameters are read in place.
+Ownership is fixed when the step is built: a Gaussian that moves into
+another rank's slab during training stays correct (it travels as halo every
+step), only less efficient; rebuild the step with `owner_of` now and then
+to re-balance.
 """
 from __future__ import annotations
 

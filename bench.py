@@ -427,9 +427,11 @@ def cpu_baseline(cfg, inputs, budget_s=12.0):
         tz0 = tz1
     return {"value": evals / secs, "unit": UNIT, "cores": O.num_threads(),
             "kind": "port",
-            "sample": f"C oracle (OpenMP), {layers} of {Tz} tile layers of the "
-                      f"same workload (projection of all {cfg.n} Gaussians + "
-                      f"slab binning, fwd, L1, bwd), {secs:.1f} s"}
+            "sample": f"C oracle (OpenMP) on the same workload: projection of "
+                      f"all {cfg.n} Gaussians, then 2-tile-layer z-slabs "
+                      f"(binning, fwd, L1, bwd) for {layers} tile layers = "
+                      f"{layers / Tz:.1f} passes over the {Tz}-layer volume, "
+                      f"{secs:.1f} s"}
 
 
 # -------------------------------------------------------------------- main

@@ -116,23 +116,31 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.file.seek(0)
-        rows = [r.split(", ") for r in self.file.read().strip().splitlines() if r.strip()]
-        sm, mx, reasons = [], 0.0, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
-                 "sw_power_cap")
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for name, flag in zip(names, r[5:9]):
-                    if flag.strip().lower() == "active":
-                        reasons.add(name)
-            except (ValueError, IndexError):
-                continue
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return parse_clock_samples(self.file.read())
+
+
+def parse_clock_samples(text: str):
+    """ClockSampler.FIELDS rows (csv, no header, no units) -> median SM
+    clock under load, the maximum SM clock and the throttle reasons that were
+    active in any sample; None without a parsable row."""
+    rows = [r.split(", ") for r in text.strip().splitlines() if r.strip()]
+    sm, mx, reasons = [], 0.0, set()
+    names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+             "sw_power_cap")
+    for r in rows:
+        try:
+            clk, clk_max = float(r[1]), float(r[2])
+        except (ValueError, IndexError):
+            continue
+        sm.append(clk)
+        mx = max(mx, clk_max)
+        for name, flag in zip(names, r[5:9]):
+            if flag.strip().lower() == "active":
+                reasons.add(name)
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+            "reasons": sorted(reasons), "samples": len(sm)}
 
 
 def setup_dist(gpus: int):

@@ -1,0 +1,40 @@
+"""Host-side helpers of bench.py that need no GPU."""
+import importlib.util
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_clock_samples_report_throttle_reasons():
+    b = _bench()
+    text = "\n".join([
+        "0, 1965, 1965, 650.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1950, 1965, 910.3, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1800, 1965, 990.0, 0x0000000000000008, Active, Not Active, Not Active, Active",
+        "garbage line",
+    ])
+    c = b.parse_clock_samples(text)
+    assert c["samples"] == 3 and c["sm_mhz"] == 1950 and c["sm_max_mhz"] == 1965
+    assert c["reasons"] == ["hw_slowdown", "sw_power_cap"]
+    assert b.parse_clock_samples("") is None
+
+
+def test_weak_workload_and_inputs_scale_with_ranks():
+    """The N-rank workload stacks N 256-deep slabs with N x 100k Gaussians
+    whose centres cover the whole stacked depth."""
+    b = _bench()
+    cfg = b.workload(4)
+    assert cfg.vol == (1024, 256, 256) and cfg.n == 400_000
+    pos, scale, quat, inten = b.make_inputs(cfg, 4)
+    zv = (pos[:, 2] - (cfg.center[0] - 0.5 * cfg.world[0])) / cfg.world[0]
+    hist = np.histogram(zv, bins=4, range=(0.0, 1.0))[0]
+    assert hist.min() > 0.2 * len(zv)  # every slab gets about a quarter

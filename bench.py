@@ -389,6 +389,31 @@ def time_main_kernels(step_obj, steps, flush):
     return res
 
 
+FALLBACK_HBM_GBS = 6650.0  # earlier measurement on this pool
+
+
+def hbm_roofline(kernel: str, ms: float, nvox: int, traffic, peaks_path=None):
+    """The dominant voxelization kernel against the measured HBM copy
+    bandwidth: algorithmic bytes = volume + target read (backward, fused L1
+    dL/dvol) or volume written + target read (forward), 8 B per voxel and
+    channel, over the kernel's average launch time."""
+    peaks_path = peaks_path or os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, source = FALLBACK_HBM_GBS, "fallback"
+    try:
+        with open(peaks_path) as f:
+            peak, source = float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        pass
+    alg = 8 * int(nvox)
+    achieved = alg / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "kernel": f"voxelize {kernel}",
+            "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": traffic,
+            "algorithmic_bytes": alg, "peak_source": f"{source} hbm_gbs",
+            "note": "compute-bound kernel (see compute_roofline): FP32 / MUFU "
+                    "arithmetic per Gaussian-voxel pair, not HBM, limits it"}
+
+
 def profiled_traffic(kernel: str, workload: str):
     """dram__bytes_read.sum + dram__bytes_write.sum per launch of the kernel
     from the committed ncu summary of this workload (profiles/), or None."""
@@ -680,14 +705,18 @@ def main():
         dom = max(kt, key=kt.get)
         achieved = E / (kt[dom] / 1e3) / 1e9
         out["kernel_ms"] = kt
-        out["roofline"] = {
+        shape = st.fstep.plan.shape if st.fstep is not None else cfg.vol
+        nvox = int(np.prod(shape)) * cfg.channels  # this rank's voxels
+        out["roofline"] = hbm_roofline(dom, kt[dom], nvox,
+                                       profiled_traffic(dom, cfg.name))
+        out["compute_roofline"] = {
             "bound": "mufu", "kernel": f"voxelize {dom}",
             "achieved": achieved, "peak": peak, "unit": "Geval/s",
             "frac": achieved / peak,
-            "traffic": profiled_traffic(dom, cfg.name),
             "note": ("one MUFU.EX2 per Gaussian-voxel evaluation at 16/clk/SM "
-                     "x 148 SMs x max SM clock; E per launch = this rank's "
-                     "forward evaluations")}
+                     "x 148 SMs x max SM clock (the FP32-pipe bound of the "
+                     "kernels' arithmetic is about the same); E per launch = "
+                     "this rank's forward evaluations")}
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small
             and not strong):
         try:

@@ -38,3 +38,17 @@ def test_weak_workload_and_inputs_scale_with_ranks():
     zv = (pos[:, 2] - (cfg.center[0] - 0.5 * cfg.world[0])) / cfg.world[0]
     hist = np.histogram(zv, bins=4, range=(0.0, 1.0))[0]
     assert hist.min() > 0.2 * len(zv)  # every slab gets about a quarter
+
+
+def test_hbm_roofline_uses_measured_peak(tmp_path):
+    b = _bench()
+    peaks = tmp_path / "peaks.json"
+    peaks.write_text('{"hbm_gbs": 6558.7}')
+    r = b.hbm_roofline("backward", 0.304, 256 ** 3, 158619648, str(peaks))
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s" and r["peak"] == 6558.7
+    assert r["algorithmic_bytes"] == 8 * 256 ** 3
+    assert abs(r["achieved"] - 8 * 256 ** 3 / 0.304e-3 / 1e9) < 1e-6
+    assert abs(r["frac"] - r["achieved"] / 6558.7) < 1e-12
+    assert r["peak_source"] == "measured hbm_gbs"
+    r = b.hbm_roofline("forward", 0.18, 100, None, str(tmp_path / "missing.json"))
+    assert r["peak"] == b.FALLBACK_HBM_GBS and r["peak_source"] == "fallback hbm_gbs"

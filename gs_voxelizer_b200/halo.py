@@ -153,7 +153,11 @@ class HaloL1Step:
         if denom is None:
             z, y, x = self.vol
             denom = float(z * y * x * self.C)
+        if denom == 0:
+            raise ValueError("denom must be non-zero")
         self.denom = float(denom)
+        if headroom < 1.0:
+            raise ValueError("headroom must be >= 1")
         self.headroom = float(headroom)
         self.use_graph = bool(use_graph)
         self.device = pos3d.device

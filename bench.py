@@ -213,10 +213,17 @@ class Step:
         self.host = [torch.from_numpy(a).pin_memory() for a in inputs]
         self.leaves = [h.to(dev).requires_grad_(True) for h in self.host]
         from gs_voxelizer_b200.workloads import phantom
-        from gs_voxelizer_b200.slab import SlabPlan, slab_bounds
-        tz0, tz1 = slab_bounds(cfg.vol, world, rank)
-        self.plan = SlabPlan(cfg.vol, tz0, tz1)
-        self.target = phantom(cfg, device=dev, z_range=(self.plan.z_begin, self.plan.z_end))
+        if impl == "reference":
+            # single GPU, whole volume; nothing of this library is loaded on
+            # the reference arm (workloads is plain numpy / torch)
+            self.plan = None
+            self.target = phantom(cfg, device=dev)
+        else:
+            from gs_voxelizer_b200.slab import SlabPlan, slab_bounds
+            tz0, tz1 = slab_bounds(cfg.vol, world, rank)
+            self.plan = SlabPlan(cfg.vol, tz0, tz1)
+            self.target = phantom(cfg, device=dev,
+                                  z_range=(self.plan.z_begin, self.plan.z_end))
         self.nvox_global = cfg.vol[0] * cfg.vol[1] * cfg.vol[2] * cfg.channels
         self.in_bytes = sum(h.numel() * h.element_size() for h in self.host)
         if impl == "reference":
@@ -316,10 +323,24 @@ class Step:
         return float(loss.detach().item())
 
     def evaluations(self):
-        """E for this rank's slab (forward pass), from a fresh binning."""
+        """E for this rank's slab (forward pass), from a fresh binning: the
+        reference extension's own binning on the reference arm, this
+        library's on the other."""
         from gs_voxelizer_b200.workloads import evaluations
-        from gs_voxelizer_b200 import cuda as C
         cfg = self.cfg
+        if self.impl == "reference":
+            ext = self.api.ext()
+            with torch.no_grad():
+                pos, scale, quat, inten = self.leaves
+                inten2 = inten if inten.dim() == 2 else inten.unsqueeze(-1)
+                pr, cq, tmin, tmax, nt = ext.optim_to_render_forward(
+                    cfg.n, pos, scale, quat, inten2, cfg.vol, cfg.world, cfg.center)
+                cum = torch.cumsum(nt, dim=0, dtype=torch.int32)
+                n_isect = int(cum[-1].item())
+                ids, bins = ext.bin_and_sort_gaussians(cfg.n, n_isect, tmin, tmax,
+                                                       cum, cfg.vol)
+                return evaluations(bins, cfg.vol), n_isect
+        from gs_voxelizer_b200 import cuda as C
         with torch.no_grad():
             pos, scale, quat, inten = self.leaves
             pr, cq, tmin, tmax, nt = C.optim_to_render_forward(
@@ -410,8 +431,10 @@ def hbm_roofline(kernel: str, ms: float, nvox: int, traffic, peaks_path=None):
             "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "traffic": traffic,
             "algorithmic_bytes": alg, "peak_source": f"{source} hbm_gbs",
-            "note": "compute-bound kernel (see compute_roofline): FP32 / MUFU "
-                    "arithmetic per Gaussian-voxel pair, not HBM, limits it"}
+            "governing": False,
+            "note": "compute-bound kernel: FP32 / MUFU arithmetic per "
+                    "Gaussian-voxel pair, not HBM, limits it; the governing "
+                    "bound is compute_roofline"}
 
 
 def profiled_traffic(kernel: str, workload: str):
@@ -428,11 +451,24 @@ def profiled_traffic(kernel: str, workload: str):
     return None
 
 
-def cpu_baseline(cfg, inputs, budget_s=12.0):
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), or the platform string."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
+def cpu_baseline(cfg, inputs, budget_s=12.0, repeats=3):
     """The C oracle (oracle/gsv_oracle.c, OpenMP) on a bounded sample of the
     same workload: consecutive 2-tile-layer z-slabs of the volume, fwd + L1 +
-    bwd, repeated over the volume until the time budget (about 12 s) is
-    used."""
+    bwd, continuing over the volume until the time budget (about 12 s) is
+    used. The budget is split into `repeats` equal runs; `value` is their
+    median and `spread` their min / max."""
     from oracle import oracle as O
     from gs_voxelizer_b200.workloads import evaluations, phantom
     pos, scale, quat, inten = inputs
@@ -441,30 +477,39 @@ def cpu_baseline(cfg, inputs, budget_s=12.0):
         pos, scale, quat, inten, cfg.vol, cfg.world, cfg.center)
     t_proj = time.perf_counter() - t0
     Tz = (cfg.vol[0] + 7) // 8
-    evals, secs, layers = 0, t_proj, 0
+    rates, layers_total, secs_total = [], 0, 0.0
     tz0 = 0
-    while secs < budget_s:
-        if tz0 >= Tz:  # whole volume done: start another pass
-            tz0 = 0
-        tz1 = min(Tz, tz0 + 2)
-        target = phantom(cfg, device="cpu", z_range=(8 * tz0, min(cfg.vol[0], 8 * tz1))).numpy()
-        t0 = time.perf_counter()
-        ids, bins = O.bin_and_sort_gaussians(tmin, tmax, cfg.vol, tile_z=(tz0, tz1))
-        vol = O.voxelize_forward(cfg.vol, ids, bins, pr, cq, inten, tile_z=(tz0, tz1))
-        _, g = O.l1_loss_and_grad(vol, target)
-        gp, gc, gi = O.voxelize_backward(cfg.vol, tmin, tmax, pr, cq, inten, g,
-                                         tile_z=(tz0, tz1))
-        secs += time.perf_counter() - t0
-        evals += 2 * evaluations(torch.from_numpy(bins), cfg.vol, (tz0, tz1))
-        layers += tz1 - tz0
-        tz0 = tz1
-    return {"value": evals / secs, "unit": UNIT, "cores": O.num_threads(),
-            "kind": "port",
+    for rep in range(repeats):
+        evals, secs, layers = 0, (t_proj if rep == 0 else 0.0), 0
+        while secs < budget_s / repeats:
+            if tz0 >= Tz:  # whole volume done: start another pass
+                tz0 = 0
+            tz1 = min(Tz, tz0 + 2)
+            target = phantom(cfg, device="cpu",
+                             z_range=(8 * tz0, min(cfg.vol[0], 8 * tz1))).numpy()
+            t0 = time.perf_counter()
+            ids, bins = O.bin_and_sort_gaussians(tmin, tmax, cfg.vol, tile_z=(tz0, tz1))
+            vol = O.voxelize_forward(cfg.vol, ids, bins, pr, cq, inten, tile_z=(tz0, tz1))
+            _, g = O.l1_loss_and_grad(vol, target)
+            gp, gc, gi = O.voxelize_backward(cfg.vol, tmin, tmax, pr, cq, inten, g,
+                                             tile_z=(tz0, tz1))
+            secs += time.perf_counter() - t0
+            evals += 2 * evaluations(torch.from_numpy(bins), cfg.vol, (tz0, tz1))
+            layers += tz1 - tz0
+            tz0 = tz1
+        rates.append(evals / secs)
+        layers_total += layers
+        secs_total += secs
+    return {"value": statistics.median(rates), "unit": UNIT,
+            "cores": O.num_threads(), "cpu_model": cpu_model(),
+            "kind": "port", "repeats": repeats,
+            "spread": {"min": min(rates), "max": max(rates)},
             "sample": f"C oracle (OpenMP) on the same workload: projection of "
                       f"all {cfg.n} Gaussians, then 2-tile-layer z-slabs "
-                      f"(binning, fwd, L1, bwd) for {layers} tile layers = "
-                      f"{layers / Tz:.1f} passes over the {Tz}-layer volume, "
-                      f"{secs:.1f} s"}
+                      f"(binning, fwd, L1, bwd) for {layers_total} tile layers = "
+                      f"{layers_total / Tz:.1f} passes over the {Tz}-layer volume "
+                      f"in {repeats} runs of ~{budget_s / repeats:.0f} s "
+                      f"({secs_total:.1f} s); value = median run"}
 
 
 # -------------------------------------------------------------------- main
@@ -599,14 +644,16 @@ def main():
         st.step()
     barrier(world)
 
-    from gs_voxelizer_b200._lib import lib
+    lib = None
+    if impl != "reference":  # the reference arm never loads libgsvox.so
+        from gs_voxelizer_b200._lib import lib
     sampler = ClockSampler(local)
     sampler.start()
-    launches0 = lib.gsv_launch_count()
+    launches0 = lib.gsv_launch_count() if lib is not None else 0
     barrier(world)
     total_ms, per = time_steps(st.step, args.steps, flush, after=st.check)
     barrier(world)
-    launches = lib.gsv_launch_count() - launches0
+    launches = lib.gsv_launch_count() - launches0 if lib is not None else 0
     if st.fstep is not None:
         # graph replays launch the captured kernels without passing through
         # the library's host launch counter
@@ -710,7 +757,7 @@ def main():
         out["roofline"] = hbm_roofline(dom, kt[dom], nvox,
                                        profiled_traffic(dom, cfg.name))
         out["compute_roofline"] = {
-            "bound": "mufu", "kernel": f"voxelize {dom}",
+            "bound": "mufu", "governing": True, "kernel": f"voxelize {dom}",
             "achieved": achieved, "peak": peak, "unit": "Geval/s",
             "frac": achieved / peak,
             "note": ("one MUFU.EX2 per Gaussian-voxel evaluation at 16/clk/SM "

@@ -717,6 +717,9 @@ int gsv_halo_unpack(int32_t n_own, int32_t C, int32_t world,
     GSV_REQUIRE(total == 0 || (recv && pos3d_radii && conics && intensities &&
                                tile_min && tile_max && flags),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    // the peers' headers (overflow bits) are read whenever there are peers
+    GSV_REQUIRE(world == 1 || (recv && flags), GSV_ERR_INVALID_ARGUMENT,
+                "%s: null pointer", fn);
     return cuda_status(gsv::launch_halo_unpack(n_own, C, R, total, recv,
                                                pos3d_radii, conics, intensities,
                                                tile_min, tile_max, flags,

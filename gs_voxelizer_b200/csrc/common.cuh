@@ -71,7 +71,6 @@ enum BwdStage { kBwdFull = 0, kBwdPrepared = 2 };
 enum ProfKind { kProfForward = 0, kProfBackwardGauss = 1, kProfBackwardVoxel = 2 };
 void profile_mark(int kind, bool stop, cudaStream_t stream);
 
-// 2^x on the special-function unit (MUFU.EX2), flush-to-zero.
 // Halo exchange of owner-sharded Gaussians (halo.cu): record sizes in
 // floats and the per-call description of the peers, passed to the kernels
 // by value.
@@ -86,6 +85,7 @@ struct HaloPeers {
     long long loff[kHaloMaxRanks];               // local index of slot 0 - n_own
 };
 
+// 2^x on the special-function unit (MUFU.EX2), flush-to-zero.
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

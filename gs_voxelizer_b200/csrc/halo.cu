@@ -149,6 +149,11 @@ halo_unpack_kernel(int n_own, int C, HaloPeers R, long long total_slots,
                    float *__restrict__ inten, int *__restrict__ tmin,
                    int *__restrict__ tmax, float *__restrict__ flags) {
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    // Every peer's segment starts with its header, also when this rank gave
+    // it no slots: thread k reads peer k's overflow bit, so a sender that
+    // had Gaussians for a zero-capacity segment is still detected.
+    if (g < R.world && g != R.rank && recv[R.off[g] * kHaloRec + 1] != 0.f)
+        flags[1] = 1.f;
     if (g >= total_slots) return;
     // source of this slot
     int s = 0;
@@ -157,7 +162,6 @@ halo_unpack_kernel(int n_own, int C, HaloPeers R, long long total_slots,
     const int slot = (int)(g - R.loff[s]);
     const float *h = recv + R.off[s] * kHaloRec;
     const int count = __float_as_int(h[0]);
-    if (slot == 0 && h[1] != 0.f) flags[1] = 1.f;  // the sender overflowed
     const long long li = n_own + g;
     if (slot < count) {
         const float *r = recv + (R.off[s] + 1 + slot) * kHaloRec;
@@ -310,8 +314,8 @@ cudaError_t launch_halo_unpack(int n_own, int C, const HaloPeers &R,
                                long long total_slots, const float *recv,
                                float *pr, float *cq, float *inten, int *tmin,
                                int *tmax, float *flags, cudaStream_t stream) {
-    if (total_slots <= 0) return cudaSuccess;
-    const unsigned blocks = (unsigned)((total_slots + 255) / 256);
+    const long long threads = std::max<long long>(total_slots, R.world);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
     halo_unpack_kernel<<<blocks, 256, 0, stream>>>(
         n_own, C, R, total_slots, recv, reinterpret_cast<float4 *>(pr),
         reinterpret_cast<float2 *>(cq), inten, tmin, tmax, flags);

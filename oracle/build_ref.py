@@ -8,7 +8,9 @@ never copied); GLM, which the reference downloads at build time
 oracle/glm_shim. Flags follow the reference's setup.py:137-149 (-O3
 --use_fast_math --expt-relaxed-constexpr) plus the sm_100a target.
 
-Usage: python oracle/build_ref.py [REFERENCE_ROOT]   (default /root/reference)
+Usage: python oracle/build_ref.py [REFERENCE_ROOT]
+REFERENCE_ROOT defaults to $GSV_REFERENCE_ROOT, else a directory named
+`reference` beside the repository's own directory.
 Output: oracle/_ref/gs_voxelizer_ref_cuda*.so (git-ignored; it travels to the
 GPU box with the repository snapshot).
 """
@@ -30,7 +32,14 @@ def built_library() -> Path | None:
     return hits[0] if hits else None
 
 
-def build(reference_root: str = "/root/reference") -> Path | None:
+def default_root() -> str:
+    """$GSV_REFERENCE_ROOT, else `reference` beside the repository."""
+    return os.environ.get("GSV_REFERENCE_ROOT",
+                          str(HERE.parent.parent / "reference"))
+
+
+def build(reference_root: str | None = None) -> Path | None:
+    reference_root = reference_root or default_root()
     src_dir = Path(reference_root) / "gs_voxelizer" / "cuda"
     if not src_dir.is_dir():
         return built_library()
@@ -79,5 +88,5 @@ def load_reference():
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else default_root()
     print(build(root))

@@ -71,7 +71,7 @@ def close(got, want, rtol, atol_rel, name):
     assert not bad.any(), f"{name}: {bad.sum()} of {bad.size} out of tolerance"
 
 
-def _run_ranks(cfg, world, arrs, target_full, shrink=False, steps=2):
+def _run_ranks(cfg, world, arrs, target_full, shrink=None, steps=2):
     from gs_voxelizer_b200.halo import HaloL1Step, owner_of
     from gs_voxelizer_b200.slab import slab_bounds
     owners = owner_of(arrs[0], cfg.vol, cfg.world, cfg.center, world)
@@ -87,9 +87,10 @@ def _run_ranks(cfg, world, arrs, target_full, shrink=False, steps=2):
             target = target_full[8 * tz0:min(cfg.vol[0], 8 * tz1)].contiguous()
             step = HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
                               comm=ThreadComm(shared, rank), use_graph=False)
-            if shrink:  # every rank: one slot per peer, so the halo overflows
-                step.caps_out = [0 if d == rank else 1 for d in range(world)]
-                step.caps_in = [0 if d == rank else 1 for d in range(world)]
+            if shrink is not None:  # every rank: `shrink` slots per peer,
+                # too few, so the halo overflows
+                step.caps_out = [0 if d == rank else shrink for d in range(world)]
+                step.caps_in = [0 if d == rank else shrink for d in range(world)]
                 step._alloc_local()
                 step._size_pairs(step.pair_cap)
             losses = [step.run() for _ in range(steps)]
@@ -147,13 +148,16 @@ def test_halo_step_matches_single_gpu(world, channels):
         assert bool((err <= 1e-5 * ref.double().abs() + 1e-6).all()), float(err.max())
 
 
-def test_halo_overflow_regrows_on_every_rank():
+@pytest.mark.parametrize("slots", [1, 0])
+def test_halo_overflow_regrows_on_every_rank(slots):
+    """Too few halo slots: one per peer, or none at all (then no record
+    slot exists and the overflow is known only from the senders' headers)."""
     from gs_voxelizer_b200.workloads import phantom
     cfg = K.small_config(vol=(64, 40, 40), n=3000, seed=81, scale=(0.01, 0.06))
     arrs = list(K.inputs(cfg))
     target = phantom(cfg, device="cuda")
     want_loss, want_grads, _ = _reference(cfg, arrs, target)
-    res = _run_ranks(cfg, 2, arrs, target, shrink=True, steps=1)
+    res = _run_ranks(cfg, 2, arrs, target, shrink=slots, steps=1)
     for r in res:
         assert r["step"].regrows == 1
         assert r["losses"][0] == pytest.approx(want_loss, rel=1e-5)

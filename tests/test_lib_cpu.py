@@ -147,3 +147,20 @@ def test_slab_bounds_partition():
                 assert b == c
             sizes = [b - a for a, b in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("channels,max_n", [(1, 349_525), (2, 349_525),
+                                            (3, 262_144), (4, 262_144)])
+def test_noalloc_limit_is_exact(channels, max_n):
+    """gsv_voxelize_forward_noalloc accepts exactly max_n Gaussians (16 MiB
+    of 48- or 64-byte records) and rejects max_n + 1. With no intersections
+    and a null output the call stops at the output check, after the size
+    check, so nothing reaches the device."""
+    from gs_voxelizer_b200._lib import i3, lib
+    fn = lib.gsv_voxelize_forward_noalloc
+    st = fn(i3((16, 16, 16)), channels, max_n, 0, None, None, None, None, None,
+            None, None)
+    assert st == 1 and "out_vol is null" in lib.gsv_last_error().decode()
+    st = fn(i3((16, 16, 16)), channels, max_n + 1, 0, None, None, None, None,
+            None, None, None)
+    assert st == 3 and "16 MiB scratch" in lib.gsv_last_error().decode()

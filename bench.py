@@ -249,6 +249,7 @@ class Step:
                 from gs_voxelizer_b200.halo import HaloL1Step, owner_of
                 owners = owner_of(inputs[0], cfg.vol, cfg.world, cfg.center, world)
                 idx = np.nonzero(owners == rank)[0]
+                self.owned_idx = idx
                 self.step_host = [torch.from_numpy(np.ascontiguousarray(a[idx])).pin_memory()
                                   for a in inputs]
                 self.step_in_bytes = sum(h.numel() * h.element_size()
@@ -512,6 +513,107 @@ def cpu_baseline(cfg, inputs, budget_s=12.0, repeats=3):
                       f"({secs_total:.1f} s); value = median run"}
 
 
+# ------------------------------------------------- multi-GPU correctness
+
+def grad_stats(got: torch.Tensor, want: torch.Tensor, floor: float = 1e-3):
+    """max |got - want| / max |want|, and the largest relative error over
+    entries above floor * max |want|."""
+    got, want = got.double(), want.double()
+    m = max(float(want.abs().max()), 1e-30)
+    d = (got - want).abs()
+    big = want.abs() > floor * m
+    rel = float((d[big] / want[big].abs()).max()) if bool(big.any()) else 0.0
+    return float(d.max()) / m, rel
+
+
+def multi_gpu_parity(st, cfg, inputs, world, rank):
+    """After the timed region (N > 1): one more step of the owner-sharded
+    halo step; the ranks' owned gradients are assembled on rank 0 (disjoint
+    rows, one NCCL sum-reduce per parameter), where the single-GPU
+    FusedL1Step over the whole volume with all Gaussians is the reference.
+    Returns {loss_rel, grad_max_rel, grad_rel_above_1e-3} on rank 0."""
+    from gs_voxelizer_b200.step import FusedL1Step
+    from gs_voxelizer_b200.workloads import phantom
+    dev = torch.device("cuda")
+    loss = st.fstep.run()
+    idx = torch.from_numpy(st.owned_idx).to(dev)
+    full = []
+    for p, a in zip(st.params, inputs):
+        g = torch.zeros((cfg.n,) + tuple(a.shape[1:]), dtype=torch.float32, device=dev)
+        if idx.numel():
+            g[idx] = p.grad.reshape((idx.numel(),) + tuple(a.shape[1:]))
+        dist.reduce(g, dst=0, op=dist.ReduceOp.SUM)
+        full.append(g)
+    out = None
+    if rank == 0:
+        params = [torch.from_numpy(a).to(dev) for a in inputs]
+        target = phantom(cfg, device=dev)
+        ref = FusedL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
+                          denom=st.nvox_global)
+        want = ref.run()
+        stats = [grad_stats(g, p.grad) for g, p in zip(full, params)]
+        out = {"reference": "single-GPU FusedL1Step, whole volume, all Gaussians",
+               "loss_rel": abs(loss - want) / abs(want),
+               "grad_max_rel": max(s[0] for s in stats),
+               "grad_rel_above_1e-3": max(s[1] for s in stats),
+               "regrows": st.fstep.regrows}
+        del ref, params, target
+    dist.barrier()
+    del full
+    torch.cuda.empty_cache()
+    return out
+
+
+def strong2048(world, rank, steps):
+    """BASELINE config 5 (2048^3, 8M Gaussians) z-slab sharded over the
+    `world` GPUs with the owner-sharded halo step at every N (N = 1: one
+    rank, no peers): strong scaling, the step replayed as CUDA graphs,
+    device-timed, max over ranks."""
+    from gs_voxelizer_b200.halo import HaloL1Step, NcclComm, owner_of
+    from gs_voxelizer_b200.slab import slab_bounds
+    from gs_voxelizer_b200.workloads import CONFIGS, evaluations, gaussians, phantom
+    cfg = CONFIGS["shard2048"]
+    dev = torch.device("cuda")
+    arrs = gaussians(cfg)
+    owners = owner_of(arrs[0], cfg.vol, cfg.world, cfg.center, world)
+    idx = np.nonzero(owners == rank)[0]
+    params = [torch.from_numpy(np.ascontiguousarray(a[idx])).to(dev) for a in arrs]
+    del arrs, owners
+    tz0, tz1 = slab_bounds(cfg.vol, world, rank)
+    target = phantom(cfg, device=dev, z_range=(8 * tz0, min(cfg.vol[0], 8 * tz1)))
+
+    class _Solo:
+        rank, world = 0, 1
+
+    step = HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
+                      comm=NcclComm() if world > 1 else _Solo())
+    for _ in range(2):
+        step.run()
+    E = evaluations(step.bins, cfg.vol, (tz0, tz1))
+    E_total = int(sum_over_ranks(float(E), world))
+    barrier(world)
+    per = []
+    for _ in range(steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step.launch()
+        e.record()
+        e.synchronize()
+        if not step.finish():
+            raise RuntimeError("config-5 step overflowed during a timed step")
+        per.append(s.elapsed_time(e))
+    ms = max_over_ranks(sum(per), world) / steps
+    out = {"workload": "shard2048", "vol_zyx": list(cfg.vol), "gaussians": cfg.n,
+           "n_gpus": world, "scaling": "strong", "steps": steps,
+           "ms_per_step": ms, "value": 2 * E_total / (ms / 1e3), "unit": UNIT,
+           "evals_per_step": 2 * E_total,
+           "step": "halo.HaloL1Step at every N (owner-sharded, halo exchange)",
+           "regrows": step.regrows}
+    del step, target, params
+    torch.cuda.empty_cache()
+    return out
+
+
 # -------------------------------------------------------------------- main
 
 def sweep_configs(kind):
@@ -578,6 +680,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the config-5 (2048^3) strong-scaling sub-record")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 128^3, 25k Gaussians, 3 steps")
     ap.add_argument("--workload", choices=["step256", "shard2048"],
@@ -764,6 +868,12 @@ def main():
                      "x 148 SMs x max SM clock (the FP32-pipe bound of the "
                      "kernels' arithmetic is about the same); E per launch = "
                      "this rank's forward evaluations")}
+    if impl != "reference" and world > 1 and not strong and not args.small:
+        out["parity"] = multi_gpu_parity(st, cfg, inputs, world, rank)
+    if impl != "reference" and not strong and not args.small and not args.no_strong:
+        del st
+        torch.cuda.empty_cache()
+        out["strong2048"] = strong2048(world, rank, steps=5)
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small
             and not strong):
         try:

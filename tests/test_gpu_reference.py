@@ -154,13 +154,15 @@ def volume_close_ties(got, want):
     contribution is alpha * I_c < 1e-6 * I_c / mean(I) <= C * 1e-6 for
     non-negative intensities. So: every voxel within 1e-5 relative plus two
     such flips, and at most one voxel per million outside the strict
-    1e-5 relative + 1e-6 absolute tolerance."""
+    1e-5 relative + 1e-6 absolute tolerance. Returns the number of voxels
+    that needed the allowance."""
     C = got.shape[-1]
     err = (got.double() - want.double()).abs()
     ref_abs = want.double().abs()
     assert bool((err <= 1e-5 * ref_abs + 2 * C * 1e-6).all()), float(err.max())
     strict = int((err > 1e-5 * ref_abs + 1e-6).sum())
     assert strict <= max(1, err.numel() // 1_000_000), (strict, err.numel())
+    return strict
 
 
 def _large_case(ref, cfg, check_backward=True):
@@ -180,7 +182,8 @@ def _large_case(ref, cfg, check_backward=True):
     assert torch.equal(ids_a, ids_b) and torch.equal(bins_a, bins_b)
     vol_a = C().voxelize_forward(cfg.vol, ids_a, bins_a, pr, cq, inten)
     vol_b = ref.voxelize_forward(cfg.vol, ids_b, bins_b, pr, cq, inten)
-    volume_close_ties(vol_a, vol_b)
+    ties = volume_close_ties(vol_a, vol_b)
+    print(f"\n[{cfg.name}] voxels on a cull-threshold tie: {ties} of {vol_a.numel()}")
     if check_backward:
         W = torch.randn(vol_a.shape, device="cuda",
                         generator=torch.Generator("cuda").manual_seed(5))

@@ -32,6 +32,8 @@ SIGNATURES = {
     "gsv_version": (ctypes.c_char_p, []),
     "gsv_launch_count": (ctypes.c_uint64, []),
     "gsv_profile_kernel": (ctypes.c_int, [_I32, _P, _P]),
+    "gsv_set_tensor_core_backward": (ctypes.c_int, [_I32]),
+    "gsv_device_error": (ctypes.c_int, [_P, _I32]),
     "gsv_optim_to_render_forward": (
         ctypes.c_int, [_I32, _I32, _P, _P, _P, _P, _I3, _F3, _F3,
                        _P, _P, _P, _P, _P, _P]),

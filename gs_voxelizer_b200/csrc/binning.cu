@@ -593,6 +593,14 @@ size_t bin_workspace_bytes(long long ntiles, long long nisect, long long n,
     return bin_layout(ntiles, nisect, n, layers).total;
 }
 
+// The pair total that the binning's scan left in its workspace.
+const long long *bin_pair_total(const void *ws, long long ntiles) {
+    const BinLayout L = bin_layout(ntiles, 0, 0, 1);
+    return reinterpret_cast<const long long *>(
+               static_cast<const char *>(ws) + L.partials) +
+           scan_blocks(ntiles);
+}
+
 long long scan_blocks(long long ntiles) {
     return (ntiles + kScanTile - 1) / kScanTile;
 }

@@ -67,6 +67,22 @@ cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
                                float *out, void *ws, cudaStream_t stream,
                                const float *target, float *loss_out,
                                double inv_denom);
+cudaError_t launch_vox_forward_ex(const Geom &g, int C, int n, long long nisect,
+                                  const int *ids, const int *tile_bins,
+                                  const float *pos_radii, const float *conics,
+                                  const float *intens, float *out, void *ws,
+                                  cudaStream_t stream, const float *target,
+                                  float *loss_out, double inv_denom,
+                                  float *sign_plane, int *tile_of);
+cudaError_t launch_vox_backward_tc(const Geom &g, const int *ids,
+                                   const int *tile_of, const float4 *rec,
+                                   const float *sign_plane,
+                                   const long long *pair_total,
+                                   long long pair_cap, float *pos_grad,
+                                   float *conic_grad, float *int_grad,
+                                   const float *grad_loss, float inv_denom,
+                                   cudaStream_t stream);
+int tc_error_flag(bool clear);
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       long long nisect, const int *ids,
                                       const int *tile_bins,
@@ -78,7 +94,9 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       cudaStream_t stream,
                                       const float *target,
                                       const float *grad_loss,
-                                      float inv_denom, int stage);
+                                      float inv_denom, int stage,
+                                      const TcInputs *tc = nullptr);
+const long long *bin_pair_total(const void *ws, long long ntiles);
 size_t l1_workspace_bytes(long long n);
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
@@ -286,6 +304,37 @@ size_t l1_bin_part(const gsv::Geom &g, long long nisect, long long n) {
     return (gsv::bin_workspace_bytes(g.slab_tiles(), nisect, n,
                                      g.slab_tiles_z()) + 255) &
            ~size_t(255);
+}
+
+// Tensor-core backward inputs (one channel): the per-tile sign plane and
+// the tile of every pair, after the binning and voxelization parts of the
+// fused-L1 workspace.
+bool g_use_tc_backward = false;
+
+bool use_tc(int C) { return C == 1 && g_use_tc_backward; }
+
+size_t l1_tc_part(const gsv::Geom &g, int C, long long nisect) {
+    if (!use_tc(C)) return 0;
+    return ((sizeof(float) * gsv::kTileVoxels * (size_t)g.slab_tiles() + 255) &
+            ~size_t(255)) +
+           ((sizeof(int) * (size_t)(nisect > 0 ? nisect : 1) + 255) & ~size_t(255));
+}
+
+struct TcBuffers {
+    float *sign_plane;
+    int *tile_of;
+};
+
+TcBuffers l1_tc_buffers(void *ws, const gsv::Geom &g, int C, int n,
+                        long long nisect) {
+    char *base = static_cast<char *>(ws) + l1_bin_part(g, nisect, n) +
+                 gsv::vox_workspace_bytes(n, C, g.slab_tiles(), nisect);
+    TcBuffers b;
+    b.sign_plane = reinterpret_cast<float *>(base);
+    b.tile_of = reinterpret_cast<int *>(
+        base + ((sizeof(float) * gsv::kTileVoxels * (size_t)g.slab_tiles() + 255) &
+                ~size_t(255)));
+    return b;
 }
 
 // halo exchange: per-peer description from the C arrays
@@ -570,7 +619,8 @@ size_t gsv_voxelize_l1_workspace_bytes(int32_t n, int32_t C, int64_t nisect,
     if (g.tz0 < 0 || g.tz1 > g.Tz || g.tz0 > g.tz1) return 0;
     const long long ni = nisect < 0 ? 0 : nisect;
     return l1_bin_part(g, ni, n < 0 ? 0 : n) +
-           gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(), ni);
+           gsv::vox_workspace_bytes(n < 0 ? 0 : n, C, g.slab_tiles(), ni) +
+           l1_tc_part(g, C, ni);
 }
 
 int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
@@ -629,9 +679,13 @@ int gsv_voxelize_forward_l1(const int32_t vol[3], int32_t tz0, int32_t tz1,
                                                 vox_ws, s),
                            fn);
     }
-    err = gsv::launch_vox_forward(g, C, n, nisect, ids_out, bins_out, pos, con, inten,
-                                  out, vox_ws, s, target, loss_out,
-                                  1.0 / (double)denom);
+    // tensor-core backward selected: also its inputs
+    TcBuffers tcb = {nullptr, nullptr};
+    if (use_tc(C)) tcb = l1_tc_buffers(ws, g, C, n, nisect);
+    err = gsv::launch_vox_forward_ex(g, C, n, nisect, ids_out, bins_out, pos,
+                                     con, inten, out, vox_ws, s, target,
+                                     loss_out, 1.0 / (double)denom,
+                                     tcb.sign_plane, tcb.tile_of);
     return cuda_status(err, fn);
 }
 
@@ -662,12 +716,36 @@ int gsv_voxelize_backward_per_gaussian_l1(
                 GSV_ERR_INVALID_ARGUMENT, "%s: null input pointer", fn);
     GSV_REQUIRE(denom != 0.f, GSV_ERR_INVALID_ARGUMENT, "%s: denom is 0", fn);
     char *vox_ws = static_cast<char *>(ws) + l1_bin_part(g, nisect, n);
+    gsv::TcInputs tc;
+    const gsv::TcInputs *tcp = nullptr;
+    if (use_tc(C)) {
+        const TcBuffers b = l1_tc_buffers(ws, g, C, n, nisect);
+        tc.sign_plane = b.sign_plane;
+        tc.tile_of = b.tile_of;
+        tc.pair_total = gsv::bin_pair_total(ws, g.slab_tiles());
+        tcp = &tc;
+    }
     return cuda_status(gsv::launch_vox_backward_gauss(
                            g, C, n, nisect, ids, bins, pos, con, inten,
                            out_vol, pos_grad, con_grad, int_grad, vox_ws,
                            as_stream(stream), target, grad_loss, 1.f / denom,
-                           gsv::kBwdPrepared),
+                           gsv::kBwdPrepared, tcp),
                        fn);
+}
+
+int gsv_set_tensor_core_backward(int32_t enable) {
+    const int prev = g_use_tc_backward ? 1 : 0;
+    g_use_tc_backward = enable != 0;
+    return prev;
+}
+
+int gsv_device_error(int32_t *flag_out, int32_t clear) {
+    const char *fn = "gsv_device_error";
+    GSV_REQUIRE(flag_out, GSV_ERR_INVALID_ARGUMENT, "%s: flag_out is null", fn);
+    const int v = gsv::tc_error_flag(clear != 0);
+    GSV_REQUIRE(v >= 0, GSV_ERR_CUDA, "%s: could not read the device flag", fn);
+    *flag_out = v;
+    return GSV_OK;
 }
 
 size_t gsv_halo_workspace_bytes(int32_t n, int32_t world) {

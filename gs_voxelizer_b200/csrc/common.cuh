@@ -62,6 +62,15 @@ struct ItemScan {
     long long cap;
 };
 
+// Inputs of the tensor-core backward (one channel, fused L1) that the fused
+// forward leaves in the workspace: the per-tile sign plane, the tile of every
+// pair and the binning's pair total.
+struct TcInputs {
+    const float *sign_plane;
+    const int *tile_of;
+    const long long *pair_total;
+};
+
 // Stages of launch_vox_backward_gauss: everything, or only the kernel (the
 // fused-L1 forward left the records and the work plan in the workspace).
 enum BwdStage { kBwdFull = 0, kBwdPrepared = 2 };

@@ -44,6 +44,14 @@ cudaError_t scan_counts_to_bins(int *counts, long long ntiles,
                                 long long *count_out = nullptr,
                                 float *overflow_out = nullptr,
                                 const ItemScan *items = nullptr);
+cudaError_t launch_vox_backward_tc(const Geom &g, const int *ids,
+                                   const int *tile_of, const float4 *rec,
+                                   const float *sign_plane,
+                                   const long long *pair_total,
+                                   long long pair_cap, float *pos_grad,
+                                   float *conic_grad, float *int_grad,
+                                   const float *grad_loss, float inv_denom,
+                                   cudaStream_t stream);
 size_t l1_workspace_bytes(long long n);
 cudaError_t launch_sum(long long n, const float *a, const float *b,
                        double inv_denom, float *out, void *ws,
@@ -169,6 +177,11 @@ __device__ __forceinline__ void fma_if_valid(float &acc, float I, float a,
 
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
+// sign(d) as -1, 0 or 1 (0 for NaN, as the L1 gradient's staging treats it)
+__device__ __forceinline__ float sign_of(float d) {
+    return d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f);
+}
+
 // sigma (log2 units) of the lane's two columns at z-offset dz:
 // s = P + dz * (L + Cz * dz), evaluated as paired FP32 FMAs (FFMA2).
 __device__ __forceinline__ float2 sigma_pair(float2 P, float2 L, float Cz,
@@ -293,7 +306,8 @@ __global__ void __launch_bounds__(32, C <= 2 ? 32 : 16)
 vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                const int *__restrict__ ids, const float4 *__restrict__ rec,
                float *__restrict__ out, const float *__restrict__ target,
-               float *__restrict__ tile_loss) {
+               float *__restrict__ tile_loss, float *__restrict__ sign_plane,
+               int *__restrict__ tile_of) {
     constexpr int R = Rec<C>::kF4;
     constexpr int RS = R + 3;  // record + 8 dz + (q, cm, mode, 1 / cm)
     constexpr int kStage = (kFwdBatch * RS * 4 > kTileVoxels * C)
@@ -316,6 +330,9 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
         for (int c = 0; c < C; ++c) acc[j][c] = make_float2(0.f, 0.f);
 
     const int2 range = bins[tile];
+    if (tile_of) {  // the tile of every pair, for the tensor-core backward
+        for (int k = range.x + lane; k < range.y; k += 32) tile_of[k] = (int)tile;
+    }
     for (int s0 = range.x; s0 < range.y; s0 += kFwdBatch) {
         const int nb = min(kFwdBatch, range.y - s0);
         __syncwarp();
@@ -391,10 +408,20 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                         (!LOSS || (reinterpret_cast<uintptr_t>(target) & 15) == 0);
     float lsum = 0.f;
+    // sign plane (C = 1, fused L1): sign(vol - target) * 2^64 per voxel of
+    // the tile, tile-major [z][y][x], 0 outside the volume
+    float4 *sp4 = (LOSS && C == 1 && sign_plane)
+                      ? reinterpret_cast<float4 *>(sign_plane + (size_t)tile * kTileVoxels)
+                      : nullptr;
+    constexpr float kSign = 18446744073709551616.f;  // 2^64
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int row = lane + 32 * h;  // 64 rows = 8 z * 8 y
         const int z = oz + (row >> 3), y = oy + (row & 7);
+        if (sp4 && !(z < g.z_end() && y < g.Y)) {
+            sp4[2 * row] = make_float4(0.f, 0.f, 0.f, 0.f);
+            sp4[2 * row + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         if (z < g.z_end() && y < g.Y) {
             const int nx = min(kTile, g.X - ox);
             const size_t base =
@@ -411,12 +438,22 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                             reinterpret_cast<const float4 *>(target + base) + q);
                         lsum += fabsf(v.x - t.x) + fabsf(v.y - t.y) +
                                 fabsf(v.z - t.z) + fabsf(v.w - t.w);
+                        if (sp4)
+                            sp4[2 * row + q] = make_float4(
+                                sign_of(v.x - t.x) * kSign, sign_of(v.y - t.y) * kSign,
+                                sign_of(v.z - t.z) * kSign, sign_of(v.w - t.w) * kSign);
                     }
                 }
             } else {
                 for (int q = 0; q < nx * C; ++q) {
                     dst[q] = src[q];
                     if (LOSS) lsum += fabsf(src[q] - __ldg(target + base + q));
+                }
+                if (sp4) {
+                    float *sp = sign_plane + (size_t)tile * kTileVoxels + row * 8;
+                    for (int q = 0; q < 8; ++q)
+                        sp[q] = q < nx ? sign_of(src[q] - __ldg(target + base + q)) * kSign
+                                       : 0.f;
                 }
             }
         }
@@ -1224,19 +1261,23 @@ static cudaError_t launch_prep(int n, int C, const float *pos_radii,
 template <int C, bool LOSS>
 static void fwd_launch(unsigned grid, cudaStream_t stream, const Geom &g,
                        const int2 *bins, const int *ids, const float4 *rec,
-                       float *out, const float *target, float *tile_loss) {
-    vox_fwd_kernel<C, LOSS><<<grid, 32, 0, stream>>>(g, bins, ids, rec, out,
-                                                     target, tile_loss);
+                       float *out, const float *target, float *tile_loss,
+                       float *sign_plane = nullptr, int *tile_of = nullptr) {
+    vox_fwd_kernel<C, LOSS><<<grid, 32, 0, stream>>>(
+        g, bins, ids, rec, out, target, tile_loss, sign_plane, tile_of);
 }
 
-// target != nullptr: fused L1, loss_out[0] = sum |vol - target| * inv_denom
-cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
+// target != nullptr: fused L1, loss_out[0] = sum |vol - target| * inv_denom;
+// sign_plane / tile_of (C = 1, fused L1, optional): the inputs of the
+// tensor-core backward (bwd_tc.cu)
+cudaError_t launch_vox_forward_ex(const Geom &g, int C, int n, long long nisect,
                                const int *ids,
                                const int *tile_bins, const float *pos_radii,
                                const float *conics, const float *intens,
                                float *out, void *ws, cudaStream_t stream,
                                const float *target, float *loss_out,
-                               double inv_denom) {
+                               double inv_denom, float *sign_plane,
+                               int *tile_of) {
     const long long ntiles = g.slab_tiles();
     // the same layout as the backward's: the fused-L1 forward's binning has
     // already written the backward's work plan into this workspace
@@ -1256,7 +1297,8 @@ cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
     const bool loss = target != nullptr;
     switch (C * 2 + (loss ? 1 : 0)) {
         case 2: fwd_launch<1, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
-        case 3: fwd_launch<1, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
+        case 3: fwd_launch<1, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss,
+                                    sign_plane, tile_of); break;
         case 4: fwd_launch<2, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
         case 5: fwd_launch<2, true>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
         case 6: fwd_launch<3, false>(grid, stream, g, bins, ids, rec, out, target, tile_loss); break;
@@ -1272,6 +1314,17 @@ cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
         return launch_sum(ntiles, tile_loss, nullptr, inv_denom, loss_out,
                           base + L.loss_partials, stream);
     return cudaSuccess;
+}
+
+cudaError_t launch_vox_forward(const Geom &g, int C, int n, long long nisect,
+                               const int *ids, const int *tile_bins,
+                               const float *pos_radii, const float *conics,
+                               const float *intens, float *out, void *ws,
+                               cudaStream_t stream, const float *target,
+                               float *loss_out, double inv_denom) {
+    return launch_vox_forward_ex(g, C, n, nisect, ids, tile_bins, pos_radii,
+                                 conics, intens, out, ws, stream, target,
+                                 loss_out, inv_denom, nullptr, nullptr);
 }
 
 // Fused-L1 forward of an empty tile list: the volume is zero, so the loss is
@@ -1355,7 +1408,8 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       cudaStream_t stream,
                                       const float *target,
                                       const float *grad_loss,
-                                      float inv_denom, int stage) {
+                                      float inv_denom, int stage,
+                                      const TcInputs *tc) {
     const long long ntiles = g.slab_tiles();
     const VoxLayout L = vox_layout(n, C, ntiles, nisect);
     char *base = static_cast<char *>(ws);
@@ -1390,6 +1444,15 @@ cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
     const long long *total = partials + nblocks;
     const float2 *cq = reinterpret_cast<const float2 *>(conics);
     const bool loss = target != nullptr;
+    if (stage == kBwdPrepared && tc && C == 1 && loss) {
+        profile_mark(kProfBackwardGauss, false, stream);
+        err = launch_vox_backward_tc(g, ids, tc->tile_of, rec, tc->sign_plane,
+                                     tc->pair_total, nisect, pos_grad,
+                                     conic_grad, int_grad, grad_loss,
+                                     inv_denom, stream);
+        profile_mark(kProfBackwardGauss, true, stream);
+        return err;
+    }
     profile_mark(kProfBackwardGauss, false, stream);
 #define GSV_BWD(Cc, Ll)                                                       \
     bwd_launch<Cc, Ll>(stream, g, ids, rec, cq, grad, item_desc, total,       \

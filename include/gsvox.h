@@ -300,6 +300,29 @@ GSV_API int gsv_voxelize_backward_per_gaussian_l1(
     void *stream);
 
 /*
+ * Backward engine of the fused-L1 step (gsv_voxelize_forward_l1 +
+ * gsv_voxelize_backward_per_gaussian_l1) for one channel: enable != 0
+ * accumulates the per-pair sums on the tensor cores (tcgen05, tensor
+ * memory), 0 (the default) selects the CUDA-core kernel, which also serves
+ * 2-4 channels and is the faster of the two on B200 at BASELINE
+ * configuration 2. With the tensor-core engine the forward also writes its
+ * inputs (a per-tile sign plane and the tile of every pair) into the
+ * workspace, which gsv_voxelize_l1_workspace_bytes then sizes larger.
+ * Process-wide; returns the previous setting. Change it only between steps
+ * and query the workspace size after it: both calls of a step and the size
+ * of their workspace must see the same setting. No reference counterpart.
+ */
+GSV_API int gsv_set_tensor_core_backward(int32_t enable);
+
+/*
+ * Device error flag of this library's kernels on the current device: 1 after
+ * a tensor-core backward launch gave up waiting on one of its internal
+ * barriers (its results are then invalid), else 0. clear != 0 resets it.
+ * Synchronises with the device. No reference counterpart.
+ */
+GSV_API int gsv_device_error(int32_t *flag_out, int32_t clear);
+
+/*
  * Forward voxelization that allocates nothing, for callers that cannot
  * provide a workspace: code whose device memory belongs to another allocator
  * (a framework that reserves the GPU's memory up front) or host programs that

@@ -34,6 +34,14 @@ SIGNATURES = {
     "gsv_profile_kernel": (ctypes.c_int, [_I32, _P, _P]),
     "gsv_set_tensor_core_backward": (ctypes.c_int, [_I32]),
     "gsv_device_error": (ctypes.c_int, [_P, _I32]),
+    "gsv_ssim3d_workspace_bytes": (ctypes.c_size_t, [_I32, _P]),
+    "gsv_ssim3d_forward": (ctypes.c_int, [_I32, _P, _P, _P, ctypes.c_float,
+                                          ctypes.c_float, _P, _P, ctypes.c_size_t, _P]),
+    "gsv_ssim3d_backward": (ctypes.c_int, [_I32, _P, _P, _P, _P, _P,
+                                           ctypes.c_size_t, _P, _P]),
+    "gsv_tv3d_workspace_bytes": (ctypes.c_size_t, [_I32, _P]),
+    "gsv_tv3d": (ctypes.c_int, [_I32, _P, _P, _I32, ctypes.c_float, _P, _P, _P,
+                                _P, ctypes.c_size_t, _P]),
     "gsv_optim_to_render_forward": (
         ctypes.c_int, [_I32, _I32, _P, _P, _P, _P, _I3, _F3, _F3,
                        _P, _P, _P, _P, _P, _P]),

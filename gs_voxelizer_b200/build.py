@@ -17,7 +17,7 @@ SRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "libgsvox.so"
 SOURCES = ["projection.cu", "binning.cu", "voxelize.cu", "bwd_tc.cu", "loss.cu",
-           "noalloc.cu", "halo.cu", "capi.cu"]
+           "ssim.cu", "noalloc.cu", "halo.cu", "capi.cu"]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

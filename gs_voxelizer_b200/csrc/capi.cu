@@ -83,6 +83,20 @@ cudaError_t launch_vox_backward_tc(const Geom &g, const int *ids,
                                    const float *grad_loss, float inv_denom,
                                    cudaStream_t stream);
 int tc_error_flag(bool clear);
+SsWindowHost ssim_window(double sigma);
+size_t ssim_workspace_bytes(int nch, int D, int H, int W);
+cudaError_t launch_ssim_forward(int nch, int D, int H, int W, const float *img1,
+                                const float *img2, float C1, float C2,
+                                const SsWindowHost &w, float *ssim_out, void *ws,
+                                cudaStream_t stream);
+cudaError_t launch_ssim_backward(int nch, int D, int H, int W, const float *img1,
+                                 const float *img2, const SsWindowHost &w,
+                                 const float *grad_out, const void *ws,
+                                 float *grad, cudaStream_t stream);
+size_t tv_workspace_bytes(int nch, int D, int H, int W);
+cudaError_t launch_tv(int nch, int D, int H, int W, const float *x, int iso,
+                      float eps, float *value_out, const float *grad_out,
+                      float *grad, void *ws, cudaStream_t stream);
 cudaError_t launch_vox_backward_gauss(const Geom &g, int C, int n,
                                       long long nisect, const int *ids,
                                       const int *tile_bins,
@@ -851,6 +865,95 @@ int gsv_halo_accumulate(int32_t n, int32_t C, int32_t world,
                            n, C, P, slot_map, recv, pos3d_radii_grad,
                            conics_grad, intensities_grad, loss, flags, out,
                            as_stream(stream)),
+                       fn);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ SSIM and TV
+
+namespace {
+
+// 0 if the planar volume description is valid, else the status (message set)
+int check_dhw(int32_t nch, const int32_t *dhw, const char *fn) {
+    if (nch < 1 || !dhw || dhw[0] <= 0 || dhw[1] <= 0 || dhw[2] <= 0)
+        return fail(GSV_ERR_INVALID_ARGUMENT, "%s: bad channel count or volume size", fn);
+    if ((long long)nch * dhw[0] * dhw[1] * dhw[2] > (1LL << 40))
+        return fail(GSV_ERR_SIZE_OVERFLOW, "%s: volume too large", fn);
+    if ((dhw[0] + 31) / 32 * (long long)nch > 65535)
+        return fail(GSV_ERR_SIZE_OVERFLOW, "%s: too many channels x z-runs", fn);
+    return GSV_OK;
+}
+
+const gsv::SsWindowHost &ssim_window_15() {
+    static const gsv::SsWindowHost w = gsv::ssim_window(1.5);
+    return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t gsv_ssim3d_workspace_bytes(int32_t channels, const int32_t dhw[3]) {
+    if (channels < 1 || !dhw || dhw[0] <= 0 || dhw[1] <= 0 || dhw[2] <= 0) return 0;
+    return gsv::ssim_workspace_bytes(channels, dhw[0], dhw[1], dhw[2]);
+}
+
+int gsv_ssim3d_forward(int32_t channels, const int32_t dhw[3], const float *img1,
+                       const float *img2, float c1, float c2, float *ssim_out,
+                       void *ws, size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_ssim3d_forward";
+    if (const int st = check_dhw(channels, dhw, fn)) return st;
+    const size_t need = gsv_ssim3d_workspace_bytes(channels, dhw);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes, need);
+    GSV_REQUIRE(img1 && img2 && ssim_out, GSV_ERR_INVALID_ARGUMENT,
+                "%s: null pointer", fn);
+    return cuda_status(gsv::launch_ssim_forward(channels, dhw[0], dhw[1], dhw[2],
+                                                img1, img2, c1, c2, ssim_window_15(),
+                                                ssim_out, ws, as_stream(stream)),
+                       fn);
+}
+
+int gsv_ssim3d_backward(int32_t channels, const int32_t dhw[3], const float *img1,
+                        const float *img2, const float *grad_out, const void *ws,
+                        size_t ws_bytes, float *grad_img1, void *stream) {
+    const char *fn = "gsv_ssim3d_backward";
+    if (const int st = check_dhw(channels, dhw, fn)) return st;
+    const size_t need = gsv_ssim3d_workspace_bytes(channels, dhw);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes, need);
+    GSV_REQUIRE(img1 && img2 && grad_out && grad_img1, GSV_ERR_INVALID_ARGUMENT,
+                "%s: null pointer", fn);
+    return cuda_status(gsv::launch_ssim_backward(channels, dhw[0], dhw[1], dhw[2],
+                                                 img1, img2, ssim_window_15(),
+                                                 grad_out, ws, grad_img1,
+                                                 as_stream(stream)),
+                       fn);
+}
+
+size_t gsv_tv3d_workspace_bytes(int32_t channels, const int32_t dhw[3]) {
+    if (channels < 1 || !dhw || dhw[0] <= 0 || dhw[1] <= 0 || dhw[2] <= 0) return 0;
+    return gsv::tv_workspace_bytes(channels, dhw[0], dhw[1], dhw[2]);
+}
+
+int gsv_tv3d(int32_t channels, const int32_t dhw[3], const float *vol,
+             int32_t isotropic, float eps, float *value_out, const float *grad_out,
+             float *grad_vol, void *ws, size_t ws_bytes, void *stream) {
+    const char *fn = "gsv_tv3d";
+    if (const int st = check_dhw(channels, dhw, fn)) return st;
+    const size_t need = gsv_tv3d_workspace_bytes(channels, dhw);
+    GSV_REQUIRE(ws && ws_bytes >= need, GSV_ERR_WORKSPACE_TOO_SMALL,
+                "%s: workspace of %zu bytes given, %zu needed", fn, ws_bytes, need);
+    GSV_REQUIRE(vol && (value_out || grad_vol), GSV_ERR_INVALID_ARGUMENT,
+                "%s: null pointer", fn);
+    GSV_REQUIRE(!grad_vol || grad_out, GSV_ERR_INVALID_ARGUMENT,
+                "%s: grad_vol needs grad_out", fn);
+    GSV_REQUIRE(!isotropic || eps > 0.f, GSV_ERR_INVALID_ARGUMENT,
+                "%s: isotropic TV needs eps > 0", fn);
+    return cuda_status(gsv::launch_tv(channels, dhw[0], dhw[1], dhw[2], vol,
+                                      isotropic, eps, value_out, grad_out, grad_vol,
+                                      ws, as_stream(stream)),
                        fn);
 }
 

@@ -71,6 +71,11 @@ struct TcInputs {
     const long long *pair_total;
 };
 
+// Normalised 11-tap Gaussian window of the 3D SSIM (host copy, ssim.cu).
+struct SsWindowHost {
+    float w[11];
+};
+
 // Stages of launch_vox_backward_gauss: everything, or only the kernel (the
 // fused-L1 forward left the records and the work plan in the workspace).
 enum BwdStage { kBwdFull = 0, kBwdPrepared = 2 };

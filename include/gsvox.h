@@ -300,6 +300,44 @@ GSV_API int gsv_voxelize_backward_per_gaussian_l1(
     void *stream);
 
 /*
+ * 3D SSIM (Wang et al. 2004) of planar volumes [channels][D][H][W]: 11^3
+ * separable Gaussian window (sigma 1.5), zero padding, constants c1, c2
+ * (the usual 0.01^2 and 0.03^2). Forward: ssim_out[0] (device float) = the
+ * mean of the SSIM map over all voxels and channels; the workspace (size
+ * from gsv_ssim3d_workspace_bytes, dhw = {D, H, W}) keeps three gradient
+ * maps for the backward. Backward (same inputs and workspace): grad_img1 =
+ * grad_out[0] * d ssim / d img1 (img2 is treated as constant).
+ * Replaces the external fused_ssim3d that the reference's tests and speed
+ * benchmarks call on the voxelized volume (test/test_gs_voxelizer.py:62,
+ * test/compare_speed.py:174); not part of the reference's sources.
+ */
+GSV_API size_t gsv_ssim3d_workspace_bytes(int32_t channels, const int32_t dhw[3]);
+GSV_API int gsv_ssim3d_forward(int32_t channels, const int32_t dhw[3],
+                               const float *img1, const float *img2, float c1,
+                               float c2, float *ssim_out, void *workspace,
+                               size_t workspace_bytes, void *stream);
+GSV_API int gsv_ssim3d_backward(int32_t channels, const int32_t dhw[3],
+                                const float *img1, const float *img2,
+                                const float *grad_out, const void *workspace,
+                                size_t workspace_bytes, float *grad_img1,
+                                void *stream);
+
+/*
+ * 3D total variation of planar volumes [channels][D][H][W] with forward
+ * differences d_a = x(v + e_a) - x(v) (0 across the far boundary):
+ * isotropic != 0: mean sqrt(dx^2 + dy^2 + dz^2 + eps) (eps > 0), else
+ * mean (|dx| + |dy| + |dz|). value_out (nullable): the value; grad_vol
+ * (nullable, needs grad_out): grad_out[0] * dTV/dvol. Replaces the external
+ * fused-3D-tv loss named beside the reference (README.md:10); not part of
+ * the reference's sources.
+ */
+GSV_API size_t gsv_tv3d_workspace_bytes(int32_t channels, const int32_t dhw[3]);
+GSV_API int gsv_tv3d(int32_t channels, const int32_t dhw[3], const float *vol,
+                     int32_t isotropic, float eps, float *value_out,
+                     const float *grad_out, float *grad_vol, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
+/*
  * Backward engine of the fused-L1 step (gsv_voxelize_forward_l1 +
  * gsv_voxelize_backward_per_gaussian_l1) for one channel: enable != 0
  * accumulates the per-pair sums on the tensor cores (tcgen05, tensor

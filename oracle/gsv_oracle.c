@@ -501,6 +501,158 @@ double oracle_l1(int64_t nvox, const float *v, const float *t, double denom,
     return s / denom;
 }
 
+/* ------------------------------------------------------------------ SSIM
+ * 3D SSIM (Wang, Bovik, Sheikh, Simoncelli 2004) as the reference's tests
+ * use it through the external fused_ssim3d (test/test_gs_voxelizer.py:62):
+ * the mean over all voxels and channels of
+ *   S = (2 mu_x mu_y + C1)(2 s_xy + C2) / ((mu_x^2 + mu_y^2 + C1)(s_x^2 + s_y^2 + C2))
+ * with local statistics under the separable window w (11 taps), zero
+ * padding. Restated from the paper's definition (the fused_ssim sources
+ * are not part of the reference); float64 throughout. grad (nullable) =
+ * d mean(S) / d img1.
+ * Volumes are planar [nch][D][H][W].
+ */
+static void blur3(int D, int H, int W, const double *w, int R, const double *in,
+                  double *out, double *tmp) {
+    const size_t plane = (size_t)H * W;
+    /* x */
+#pragma omp parallel for
+    for (long long zy = 0; zy < (long long)D * H; ++zy)
+        for (int x = 0; x < W; ++x) {
+            double acc = 0.0;
+            for (int k = -R; k <= R; ++k)
+                if (x + k >= 0 && x + k < W) acc += w[k + R] * in[zy * W + x + k];
+            out[zy * W + x] = acc;
+        }
+    /* y */
+#pragma omp parallel for
+    for (long long z = 0; z < D; ++z)
+        for (int y = 0; y < H; ++y)
+            for (int x = 0; x < W; ++x) {
+                double acc = 0.0;
+                for (int k = -R; k <= R; ++k)
+                    if (y + k >= 0 && y + k < H)
+                        acc += w[k + R] * out[z * plane + (size_t)(y + k) * W + x];
+                tmp[z * plane + (size_t)y * W + x] = acc;
+            }
+    /* z */
+#pragma omp parallel for
+    for (long long z = 0; z < D; ++z)
+        for (size_t q = 0; q < plane; ++q) {
+            double acc = 0.0;
+            for (int k = -R; k <= R; ++k)
+                if (z + k >= 0 && z + k < D) acc += w[k + R] * tmp[(z + k) * plane + q];
+            out[z * plane + q] = acc;
+        }
+}
+
+double oracle_ssim3d(int nch, int D, int H, int W, const float *a, const float *b,
+                     double C1, double C2, const double *w, int R, float *grad) {
+    const size_t nv = (size_t)D * H * W;
+    const double inv_n = 1.0 / ((double)nv * nch);
+    double *in = malloc(sizeof(double) * nv), *tmp = malloc(sizeof(double) * nv);
+    double *m[5];
+    for (int k = 0; k < 5; ++k) m[k] = malloc(sizeof(double) * nv);
+    double total = 0.0;
+    for (int c = 0; c < nch; ++c) {
+        const float *x = a + c * nv, *y = b + c * nv;
+        for (int k = 0; k < 5; ++k) {
+            for (size_t i = 0; i < nv; ++i) {
+                const double xv = x[i], yv = y[i];
+                in[i] = k == 0 ? xv : k == 1 ? yv : k == 2 ? xv * xv
+                      : k == 3 ? yv * yv : xv * yv;
+            }
+            blur3(D, H, W, w, R, in, m[k], tmp);
+        }
+        /* S and the three G maps (for d mean / d S = 1/N) in m[2..4] */
+        double part = 0.0;
+        for (size_t i = 0; i < nv; ++i) {
+            const double mx = m[0][i], my = m[1][i];
+            const double sxx = m[2][i] - mx * mx, syy = m[3][i] - my * my,
+                         sxy = m[4][i] - mx * my;
+            const double A1 = 2 * mx * my + C1, A2 = 2 * sxy + C2;
+            const double B1 = mx * mx + my * my + C1, B2 = sxx + syy + C2;
+            const double S = A1 * A2 / (B1 * B2);
+            part += S;
+            m[2][i] = inv_n * (2 * my * (A2 - A1) / (B1 * B2) +
+                               2 * mx * S * (1.0 / B2 - 1.0 / B1));
+            m[3][i] = inv_n * (-S / B2);
+            m[4][i] = inv_n * (2 * A1 / (B1 * B2));
+        }
+        total += part;
+        if (grad) {
+            float *g = grad + c * nv;
+            blur3(D, H, W, w, R, m[2], m[0], tmp);
+            blur3(D, H, W, w, R, m[3], m[1], tmp);
+            blur3(D, H, W, w, R, m[4], m[2], tmp);
+            for (size_t i = 0; i < nv; ++i)
+                g[i] = (float)(m[0][i] + 2.0 * x[i] * m[1][i] + y[i] * m[2][i]);
+        }
+    }
+    free(in);
+    free(tmp);
+    for (int k = 0; k < 5; ++k) free(m[k]);
+    return total * inv_n;
+}
+
+/* -------------------------------------------------------------------- TV
+ * 3D total variation (Rudin, Osher, Fatemi 1992) with forward differences
+ * d_a(v) = x(v + e_a) - x(v) inside the volume (0 across the far edge):
+ * iso: mean sqrt(dx^2 + dy^2 + dz^2 + eps); else mean (|dx| + |dy| + |dz|).
+ * The companion external package (fused-3D-tv) is not part of the
+ * reference; restated from the definition, float64. grad (nullable) =
+ * d TV / d x. Planar [nch][D][H][W].
+ */
+static void tv_diff(const float *x, int D, int H, int W, int z, int y, int xx,
+                    double *d) {
+    const size_t i = ((size_t)z * H + y) * W + xx;
+    d[0] = xx + 1 < W ? (double)x[i + 1] - x[i] : 0.0;
+    d[1] = y + 1 < H ? (double)x[i + W] - x[i] : 0.0;
+    d[2] = z + 1 < D ? (double)x[i + (size_t)H * W] - x[i] : 0.0;
+}
+
+static double tv_term(const double *d, int iso, double eps) {
+    return iso ? sqrt(d[0] * d[0] + d[1] * d[1] + d[2] * d[2] + eps)
+               : fabs(d[0]) + fabs(d[1]) + fabs(d[2]);
+}
+
+static double sgn(double v) { return (v > 0) - (v < 0); }
+
+double oracle_tv3d(int nch, int D, int H, int W, const float *xs, int iso,
+                   double eps, float *grad) {
+    const size_t nv = (size_t)D * H * W;
+    const double inv_n = 1.0 / ((double)nv * nch);
+    double total = 0.0;
+    for (int c = 0; c < nch; ++c) {
+        const float *x = xs + c * nv;
+        double part = 0.0;
+#pragma omp parallel for reduction(+ : part)
+        for (long long z = 0; z < D; ++z)
+            for (int y = 0; y < H; ++y)
+                for (int xx = 0; xx < W; ++xx) {
+                    double d[3];
+                    tv_diff(x, D, H, W, (int)z, y, xx, d);
+                    const double t = tv_term(d, iso, eps);
+                    part += t;
+                    if (!grad) continue;
+                    double g = iso ? -(d[0] + d[1] + d[2]) / t
+                                   : -(sgn(d[0]) + sgn(d[1]) + sgn(d[2]));
+                    const int nz[3][3] = {{0, 0, -1}, {0, -1, 0}, {-1, 0, 0}};
+                    for (int a = 0; a < 3; ++a) {  /* neighbours behind v */
+                        const int zz = (int)z + nz[a][0], yy = y + nz[a][1],
+                                  xw = xx + nz[a][2];
+                        if (zz < 0 || yy < 0 || xw < 0) continue;
+                        double e[3];
+                        tv_diff(x, D, H, W, zz, yy, xw, e);
+                        g += iso ? e[a] / tv_term(e, 1, eps) : sgn(e[a]);
+                    }
+                    grad[c * nv + ((size_t)z * H + y) * W + xx] = (float)(g * inv_n);
+                }
+        total += part;
+    }
+    return total * inv_n;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     extern int omp_get_max_threads(void);

@@ -40,6 +40,10 @@ def lib():
         L.oracle_vox_bwd.restype = None
         L.oracle_l1.argtypes = [i64, P, P, f64, P]
         L.oracle_l1.restype = f64
+        L.oracle_ssim3d.argtypes = [i32, i32, i32, i32, P, P, f64, f64, P, i32, P]
+        L.oracle_ssim3d.restype = f64
+        L.oracle_tv3d.argtypes = [i32, i32, i32, i32, P, i32, f64, P]
+        L.oracle_tv3d.restype = f64
         L.oracle_num_threads.argtypes = []
         L.oracle_num_threads.restype = i32
         _lib = L
@@ -176,3 +180,33 @@ def l1_loss_and_grad(vol, target):
     g = np.empty_like(v)
     loss = lib().oracle_l1(v.size, _p(v), _p(t), float(v.size), _p(g))
     return loss, g
+
+
+def ssim_window(sigma: float = 1.5, radius: int = 5) -> np.ndarray:
+    """Normalised 1-D Gaussian window of 2 * radius + 1 taps (float64)."""
+    k = np.arange(-radius, radius + 1, dtype=np.float64)
+    w = np.exp(-k * k / (2.0 * sigma * sigma))
+    return w / w.sum()
+
+
+def ssim3d(img1, img2, c1=0.01 ** 2, c2=0.03 ** 2, grad=True):
+    """Mean 3D SSIM of planar volumes [..., D, H, W] (leading dims are
+    channels) and, with grad, d SSIM / d img1 (float32, same shape)."""
+    a, b = _f32(img1), _f32(img2)
+    D, H, W = a.shape[-3:]
+    nch = int(np.prod(a.shape[:-3])) if a.ndim > 3 else 1
+    w = np.ascontiguousarray(ssim_window(), dtype=np.float64)
+    g = np.empty_like(a) if grad else None
+    v = lib().oracle_ssim3d(nch, D, H, W, _p(a), _p(b), c1, c2, _p(w), 5, _p(g))
+    return (v, g) if grad else v
+
+
+def tv3d(vol, isotropic=True, eps=1e-8, grad=True):
+    """3D total variation (mean over voxels and channels) of planar volumes
+    [..., D, H, W] and, with grad, its gradient."""
+    x = _f32(vol)
+    D, H, W = x.shape[-3:]
+    nch = int(np.prod(x.shape[:-3])) if x.ndim > 3 else 1
+    g = np.empty_like(x) if grad else None
+    v = lib().oracle_tv3d(nch, D, H, W, _p(x), 1 if isotropic else 0, eps, _p(g))
+    return (v, g) if grad else v

@@ -564,6 +564,76 @@ def multi_gpu_parity(st, cfg, inputs, world, rank):
     return out
 
 
+def profile_variant_step(variant, cfg, inputs):
+    """A drop-in-API training step for --profile-run: per-voxel backward
+    with the L1 loss ("voxel"), or the per-Gaussian backward with
+    1 - fused_ssim3d ("ssim")."""
+    from gs_voxelizer_b200.losses import fused_ssim3d
+    from gs_voxelizer_b200.optim_to_render import optim_to_render
+    from gs_voxelizer_b200.voxelize import voxelize_gaussians
+    from gs_voxelizer_b200.workloads import phantom
+    dev = torch.device("cuda")
+    target = phantom(cfg, device=dev)
+    leaves = [torch.from_numpy(a).to(dev).requires_grad_(True) for a in inputs]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        pr, cq, tmin, tmax, nt = optim_to_render(*leaves, cfg.vol, cfg.world,
+                                                 cfg.center)
+        vol = voxelize_gaussians(pr, cq, leaves[3], cfg.vol, tmin, tmax, nt,
+                                 use_per_gaussian_backward=variant != "voxel")
+        if variant == "ssim":
+            loss = 1.0 - fused_ssim3d(vol.squeeze().unsqueeze(0).unsqueeze(0),
+                                      target[..., 0][None, None])
+        else:
+            loss = torch.nn.functional.l1_loss(vol, target)
+        loss.backward()
+    return step
+
+
+def ssim_step(cfg, inputs, steps, flush):
+    """BASELINE configuration 2 trained with the 3D SSIM loss the reference's
+    own tests put after the voxelizer (test/test_gs_voxelizer.py:62):
+    optim_to_render -> voxelize_gaussians -> 1 - fused_ssim3d([1,1,Z,Y,X])
+    -> backward, through autograd, per-step CUDA events with the L2 flushed
+    between steps. Also the SSIM kernels alone on the same volume."""
+    from gs_voxelizer_b200.losses import fused_ssim3d
+    from gs_voxelizer_b200.optim_to_render import optim_to_render
+    from gs_voxelizer_b200.voxelize import voxelize_gaussians
+    from gs_voxelizer_b200.workloads import phantom
+    dev = torch.device("cuda")
+    target = phantom(cfg, device=dev)[..., 0][None, None].contiguous()
+    leaves = [torch.from_numpy(a).to(dev).requires_grad_(True) for a in inputs]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        pr, cq, tmin, tmax, nt = optim_to_render(*leaves, cfg.vol, cfg.world,
+                                                 cfg.center)
+        vol = voxelize_gaussians(pr, cq, leaves[3], cfg.vol, tmin, tmax, nt)
+        loss = 1.0 - fused_ssim3d(vol.squeeze().unsqueeze(0).unsqueeze(0), target)
+        loss.backward()
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    _, per = time_steps(step, steps, flush)
+    vol = torch.rand_like(target).requires_grad_(True)
+
+    def ssim_only():
+        fused_ssim3d(vol, target).backward()
+
+    for _ in range(3):
+        ssim_only()
+    _, per_ssim = time_steps(ssim_only, steps, flush)
+    return {"workload": cfg.name, "loss": "1 - fused_ssim3d (11^3 window)",
+            "ms_per_step": statistics.median(per),
+            "ssim_fwd_bwd_ms": statistics.median(per_ssim),
+            "api": "optim_to_render + voxelize_gaussians + losses.fused_ssim3d "
+                   "+ backward (autograd)"}
+
+
 def strong2048(world, rank, steps):
     """BASELINE config 5 (2048^3, 8M Gaussians) z-slab sharded over the
     `world` GPUs with the owner-sharded halo step at every N (N = 1: one
@@ -694,6 +764,12 @@ def main():
                          "(volume x channel sweep): one JSON line per case")
     ap.add_argument("--profile-run", action="store_true",
                     help="only run warmup + steps training steps (for ncu), print no JSON")
+    ap.add_argument("--variant", choices=["graph", "fused", "dropin", "voxel", "ssim"],
+                    default="graph",
+                    help="--profile-run step: graph (the timed FusedL1Step), fused "
+                         "(autograd, fused L1), dropin (voxelize_gaussians + torch "
+                         "L1), voxel (dropin with the per-voxel backward), ssim "
+                         "(dropin with 1 - fused_ssim3d)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -733,11 +809,16 @@ def main():
     st = Step(impl, cfg, world, rank, inputs)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     if args.profile_run:
+        fn = st.step
+        if args.variant in ("fused", "dropin"):
+            st.mode = args.variant
+        elif args.variant in ("voxel", "ssim"):
+            fn = profile_variant_step(args.variant, cfg, inputs)
         for _ in range(args.warmup + args.steps):
             flush.fill_(1.0)
-            st.step()
+            fn()
         torch.cuda.synchronize()
-        log(f"profile run: {args.warmup + args.steps} steps of {cfg.name}")
+        log(f"profile run: {args.warmup + args.steps} {args.variant} steps of {cfg.name}")
         return
 
     E, n_isect = st.evaluations()
@@ -870,6 +951,8 @@ def main():
                      "this rank's forward evaluations")}
     if impl != "reference" and world > 1 and not strong and not args.small:
         out["parity"] = multi_gpu_parity(st, cfg, inputs, world, rank)
+    if impl != "reference" and world == 1 and not strong and not args.small:
+        out["ssim_step"] = ssim_step(cfg, inputs, max(5, min(args.steps, 20)), flush)
     if impl != "reference" and not strong and not args.small and not args.no_strong:
         del st
         torch.cuda.empty_cache()

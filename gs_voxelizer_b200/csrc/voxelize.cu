@@ -309,7 +309,10 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
                float *__restrict__ tile_loss, float *__restrict__ sign_plane,
                int *__restrict__ tile_of) {
     constexpr int R = Rec<C>::kF4;
-    constexpr int RS = R + 3;  // record + 8 dz + (q, cm, mode, 1 / cm)
+    // record + 8 dz + (q, cm, mode, 1 / cm), padded to 7 float4 (112 B):
+    // with a 28-word stride the eight float4 stores of a quarter-warp hit
+    // eight different bank groups
+    constexpr int RS = 7;
     constexpr int kStage = (kFwdBatch * RS * 4 > kTileVoxels * C)
                                ? kFwdBatch * RS * 4
                                : kTileVoxels * C;
@@ -408,6 +411,43 @@ vox_fwd_kernel(Geom g, const int2 *__restrict__ bins,
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0) &&
                         (!LOSS || (reinterpret_cast<uintptr_t>(target) & 15) == 0);
     float lsum = 0.f;
+    if (C == 1 && vec_ok && oz + kTile <= g.z_end() && oy + kTile <= g.Y &&
+        ox + kTile <= g.X && (g.X & 3) == 0) {
+        // interior tile, one channel: lane l takes float4 l + 32 h of the
+        // staged block (rows of 8 voxels, two float4 each), so consecutive
+        // lanes read consecutive shared-memory words
+        float4 *sp4 = (LOSS && sign_plane)
+                          ? reinterpret_cast<float4 *>(sign_plane + (size_t)tile * kTileVoxels)
+                          : nullptr;
+        constexpr float kSign = 18446744073709551616.f;  // 2^64
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int f = lane + 32 * h;       // float4 index in the block
+            const int row = f >> 1, q = f & 1;  // row = 8 z + y
+            const int z = oz + (row >> 3), y = oy + (row & 7);
+            const size_t base =
+                ((size_t)(z - g.z_begin()) * g.Y + y) * g.X + ox + 4 * q;
+            const float4 v = reinterpret_cast<const float4 *>(smem)[f];
+            *reinterpret_cast<float4 *>(out + base) = v;
+            if (LOSS) {
+                const float4 t = __ldg(reinterpret_cast<const float4 *>(target + base));
+                lsum += fabsf(v.x - t.x) + fabsf(v.y - t.y) + fabsf(v.z - t.z) +
+                        fabsf(v.w - t.w);
+                if (sp4)
+                    sp4[f] = make_float4(sign_of(v.x - t.x) * kSign,
+                                         sign_of(v.y - t.y) * kSign,
+                                         sign_of(v.z - t.z) * kSign,
+                                         sign_of(v.w - t.w) * kSign);
+            }
+        }
+        if (LOSS) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            if (lane == 0) tile_loss[tile] = lsum;
+        }
+        return;
+    }
     // sign plane (C = 1, fused L1): sign(vol - target) * 2^64 per voxel of
     // the tile, tile-major [z][y][x], 0 outside the volume
     float4 *sp4 = (LOSS && C == 1 && sign_plane)

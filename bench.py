@@ -57,6 +57,7 @@ UNIT = "evals/s"
 SMS = 148
 MUFU_PER_CLK = 16          # MUFU.EX2 throughput per SM per clock
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+EXCHANGE = "p2p"  # halo exchange at N > 1 (--exchange)
 
 
 # ----------------------------------------------------------------- helpers
@@ -257,7 +258,8 @@ class Step:
                 self.params = [h.to(dev) for h in self.step_host]
                 self.fstep = HaloL1Step(*self.params, cfg.vol, cfg.world,
                                         cfg.center, self.target,
-                                        denom=self.nvox_global)
+                                        denom=self.nvox_global,
+                                        exchange=EXCHANGE)
             else:
                 from gs_voxelizer_b200.step import FusedL1Step
                 self.params = [h.to(dev) for h in self.host]
@@ -639,7 +641,7 @@ def strong2048(world, rank, steps):
     `world` GPUs with the owner-sharded halo step at every N (N = 1: one
     rank, no peers): strong scaling, the step replayed as CUDA graphs,
     device-timed, max over ranks."""
-    from gs_voxelizer_b200.halo import HaloL1Step, NcclComm, owner_of
+    from gs_voxelizer_b200.halo import HaloL1Step, owner_of
     from gs_voxelizer_b200.slab import slab_bounds
     from gs_voxelizer_b200.workloads import CONFIGS, evaluations, gaussians, phantom
     cfg = CONFIGS["shard2048"]
@@ -656,7 +658,7 @@ def strong2048(world, rank, steps):
         rank, world = 0, 1
 
     step = HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
-                      comm=NcclComm() if world > 1 else _Solo())
+                      comm=None if world > 1 else _Solo(), exchange=EXCHANGE)
     for _ in range(2):
         step.run()
     E = evaluations(step.bins, cfg.vol, (tz0, tz1))
@@ -770,8 +772,14 @@ def main():
                          "(autograd, fused L1), dropin (voxelize_gaussians + torch "
                          "L1), voxel (dropin with the per-voxel backward), ssim "
                          "(dropin with 1 - fused_ssim3d)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="halo exchange at N > 1: direct writes into the peers' "
+                         "symmetric receive buffers + device barriers (p2p), or "
+                         "two NCCL all-to-alls per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global EXCHANGE
+    EXCHANGE = args.exchange
 
     world, rank, local = setup_dist(args.gpus)
     impl = args.impl
@@ -906,7 +914,11 @@ def main():
                                  "kernels"),
                    "step": ("reference API through autograd" if impl == "reference"
                             else "gs_voxelizer_b200.halo.HaloL1Step: sync-free, "
-                                 "3 CUDA graphs around 2 NCCL all-to-alls" if world > 1
+                                 "3 CUDA graphs around 2 exchanges ("
+                                 + ("direct writes into the peers' symmetric "
+                                    "receive buffers + device barriers"
+                                    if EXCHANGE == "p2p" else "NCCL all-to-alls")
+                                 + ")" if world > 1
                             else "gs_voxelizer_b200.step.FusedL1Step: sync-free, "
                                  "replayed as a CUDA graph")},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,

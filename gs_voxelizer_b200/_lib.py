@@ -95,6 +95,13 @@ SIGNATURES = {
     "gsv_halo_unpack": (
         ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
                        _P, _P]),
+    "gsv_peer_barrier": (ctypes.c_int, [_I32, _I32, _P, _P, _P]),
+    "gsv_halo_pack_peers": (
+        ctypes.c_int, [_I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _P, _P,
+                       _P, _P, _P, _P, _SZ, _P]),
+    "gsv_halo_pack_grads_peers": (
+        ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                       _P]),
     "gsv_halo_pack_grads": (
         ctypes.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
                        _P]),

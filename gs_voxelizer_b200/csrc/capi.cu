@@ -37,7 +37,7 @@ ItemScan vox_item_scan(void *ws, long long n, int C, long long ntiles,
 size_t halo_workspace_bytes(int n, int world);
 cudaError_t launch_halo_pack(int n, int C, const float *pr, const float *cq,
                              const float *inten, const int *tmin,
-                             const int *tmax, const HaloPeers &P, float *send,
+                             const int *tmax, const HaloPeers &P,
                              int *slot_map, long long *counts_out, void *ws,
                              cudaStream_t stream);
 cudaError_t launch_halo_unpack(int n_own, int C, const HaloPeers &R,
@@ -48,7 +48,7 @@ cudaError_t launch_halo_pack_grads(int n_own, int C, const HaloPeers &R,
                                    long long total_slots, const float *gp,
                                    const float *gc, const float *gi,
                                    const float *loss, const float *flags,
-                                   float *send, cudaStream_t stream);
+                                   cudaStream_t stream);
 cudaError_t launch_halo_accumulate(int n, int C, const HaloPeers &P,
                                    const int *slot_map, const float *recv,
                                    float *gp, float *gc, float *gi,
@@ -83,6 +83,9 @@ cudaError_t launch_vox_backward_tc(const Geom &g, const int *ids,
                                    const float *grad_loss, float inv_denom,
                                    cudaStream_t stream);
 int tc_error_flag(bool clear);
+int peer_error_flag(bool clear);
+cudaError_t launch_peer_barrier(int world, int rank, const long long *sig_ptrs,
+                                int *epoch, cudaStream_t stream);
 SsWindowHost ssim_window(double sigma);
 size_t ssim_workspace_bytes(int nch, int D, int H, int W);
 cudaError_t launch_ssim_forward(int nch, int D, int H, int W, const float *img1,
@@ -349,6 +352,25 @@ TcBuffers l1_tc_buffers(void *ws, const gsv::Geom &g, int C, int n,
         base + ((sizeof(float) * gsv::kTileVoxels * (size_t)g.slab_tiles() + 255) &
                 ~size_t(255)));
     return b;
+}
+
+// halo exchange: segment destinations, in a local send buffer (send + the
+// segment's record offset) or given directly (seg_dst, device addresses in
+// the peers' receive buffers); false if a needed one is missing
+bool set_destinations(gsv::HaloPeers &P, float *send, const int64_t *seg_dst,
+                      int rec) {
+    for (int d = 0; d < P.world; ++d) {
+        P.dst[d] = nullptr;
+        if (d == P.rank) continue;
+        if (seg_dst) {
+            P.dst[d] = reinterpret_cast<float *>(static_cast<uintptr_t>(seg_dst[d]));
+            if (!P.dst[d] || (seg_dst[d] & 15)) return false;
+        } else {
+            if (!send) return false;
+            P.dst[d] = send + P.off[d] * rec;
+        }
+    }
+    return true;
 }
 
 // halo exchange: per-peer description from the C arrays
@@ -756,9 +778,11 @@ int gsv_set_tensor_core_backward(int32_t enable) {
 int gsv_device_error(int32_t *flag_out, int32_t clear) {
     const char *fn = "gsv_device_error";
     GSV_REQUIRE(flag_out, GSV_ERR_INVALID_ARGUMENT, "%s: flag_out is null", fn);
-    const int v = gsv::tc_error_flag(clear != 0);
-    GSV_REQUIRE(v >= 0, GSV_ERR_CUDA, "%s: could not read the device flag", fn);
-    *flag_out = v;
+    const int a = gsv::tc_error_flag(clear != 0);
+    const int b = gsv::peer_error_flag(clear != 0);
+    GSV_REQUIRE(a >= 0 && b >= 0, GSV_ERR_CUDA, "%s: could not read the device flags",
+                fn);
+    *flag_out = (a ? 1 : 0) | (b ? 2 : 0);
     return GSV_OK;
 }
 
@@ -767,14 +791,15 @@ size_t gsv_halo_workspace_bytes(int32_t n, int32_t world) {
     return gsv::halo_workspace_bytes(n, world);
 }
 
-int gsv_halo_pack(int32_t n, int32_t C, const float *pos3d_radii,
-                          const float *conics, const float *intensities,
-                          const int32_t *tile_min, const int32_t *tile_max,
-                          int32_t world, int32_t rank, const int32_t *slab_tz,
-                          const int64_t *seg_off, const int32_t *seg_slots,
-                          float *send, int32_t *slot_map, int64_t *counts_out,
-                          void *ws, size_t ws_bytes, void *stream) {
-    const char *fn = "gsv_halo_pack";
+static int halo_pack_impl(const char *fn, int32_t n, int32_t C,
+                          const float *pos3d_radii, const float *conics,
+                          const float *intensities, const int32_t *tile_min,
+                          const int32_t *tile_max, int32_t world, int32_t rank,
+                          const int32_t *slab_tz, const int64_t *seg_off,
+                          const int32_t *seg_slots, float *send,
+                          const int64_t *seg_dst, int32_t *slot_map,
+                          int64_t *counts_out, void *ws, size_t ws_bytes,
+                          void *stream) {
     gsv::HaloPeers P;
     long long total;
     GSV_REQUIRE(n >= 0 && C >= 1 && C <= 4 && slab_tz &&
@@ -782,16 +807,45 @@ int gsv_halo_pack(int32_t n, int32_t C, const float *pos3d_radii,
                 GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
     GSV_REQUIRE(ws && ws_bytes >= gsv::halo_workspace_bytes(n, world),
                 GSV_ERR_WORKSPACE_TOO_SMALL, "%s: workspace too small", fn);
-    GSV_REQUIRE(send && slot_map &&
-                    (n == 0 || (pos3d_radii && conics && intensities &&
-                                tile_min && tile_max)),
+    GSV_REQUIRE(slot_map && (n == 0 || (pos3d_radii && conics && intensities &&
+                                        tile_min && tile_max)),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    GSV_REQUIRE(set_destinations(P, send, seg_dst, gsv::kHaloRec),
+                GSV_ERR_INVALID_ARGUMENT,
+                "%s: missing or misaligned segment destination", fn);
     return cuda_status(gsv::launch_halo_pack(n, C, pos3d_radii, conics,
                                              intensities, tile_min, tile_max,
-                                             P, send, slot_map,
+                                             P, slot_map,
                                              reinterpret_cast<long long *>(counts_out),
                                              ws, as_stream(stream)),
                        fn);
+}
+
+int gsv_halo_pack(int32_t n, int32_t C, const float *pos3d_radii,
+                  const float *conics, const float *intensities,
+                  const int32_t *tile_min, const int32_t *tile_max,
+                  int32_t world, int32_t rank, const int32_t *slab_tz,
+                  const int64_t *seg_off, const int32_t *seg_slots,
+                  float *send, int32_t *slot_map, int64_t *counts_out,
+                  void *ws, size_t ws_bytes, void *stream) {
+    return halo_pack_impl("gsv_halo_pack", n, C, pos3d_radii, conics,
+                          intensities, tile_min, tile_max, world, rank, slab_tz,
+                          seg_off, seg_slots, send, nullptr, slot_map,
+                          counts_out, ws, ws_bytes, stream);
+}
+
+int gsv_halo_pack_peers(int32_t n, int32_t C, const float *pos3d_radii,
+                        const float *conics, const float *intensities,
+                        const int32_t *tile_min, const int32_t *tile_max,
+                        int32_t world, int32_t rank, const int32_t *slab_tz,
+                        const int64_t *seg_off, const int32_t *seg_slots,
+                        const int64_t *seg_dst, int32_t *slot_map,
+                        int64_t *counts_out, void *ws, size_t ws_bytes,
+                        void *stream) {
+    return halo_pack_impl("gsv_halo_pack_peers", n, C, pos3d_radii, conics,
+                          intensities, tile_min, tile_max, world, rank, slab_tz,
+                          seg_off, seg_slots, nullptr, seg_dst, slot_map,
+                          counts_out, ws, ws_bytes, stream);
 }
 
 int gsv_halo_unpack(int32_t n_own, int32_t C, int32_t world,
@@ -819,29 +873,55 @@ int gsv_halo_unpack(int32_t n_own, int32_t C, int32_t world,
                        fn);
 }
 
-int gsv_halo_pack_grads(int32_t n_own, int32_t C, int32_t world,
-                                int32_t rank, const int64_t *seg_off,
-                                const int32_t *seg_slots,
+static int halo_pack_grads_impl(const char *fn, int32_t n_own, int32_t C,
+                                int32_t world, int32_t rank,
+                                const int64_t *seg_off, const int32_t *seg_slots,
                                 const float *pos3d_radii_grad,
                                 const float *conics_grad,
-                                const float *intensities_grad,
-                                const float *loss, const float *flags,
-                                float *send, void *stream) {
-    const char *fn = "gsv_halo_pack_grads";
+                                const float *intensities_grad, const float *loss,
+                                const float *flags, float *send,
+                                const int64_t *seg_dst, void *stream) {
     gsv::HaloPeers R;
     long long total;
     GSV_REQUIRE(n_own >= 0 && C >= 1 && C <= 4 &&
                     make_peers(world, rank, nullptr, seg_off, seg_slots, R, total),
                 GSV_ERR_INVALID_ARGUMENT, "%s: bad sizes or peer description", fn);
-    GSV_REQUIRE(send && loss && flags &&
+    GSV_REQUIRE(loss && flags &&
                     (total == 0 || (pos3d_radii_grad && conics_grad &&
                                     intensities_grad)),
                 GSV_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
+    GSV_REQUIRE(set_destinations(R, send, seg_dst, gsv::kHaloGrad),
+                GSV_ERR_INVALID_ARGUMENT,
+                "%s: missing or misaligned segment destination", fn);
     return cuda_status(gsv::launch_halo_pack_grads(
                            n_own, C, R, total, pos3d_radii_grad, conics_grad,
-                           intensities_grad, loss, flags, send,
-                           as_stream(stream)),
+                           intensities_grad, loss, flags, as_stream(stream)),
                        fn);
+}
+
+int gsv_halo_pack_grads(int32_t n_own, int32_t C, int32_t world, int32_t rank,
+                        const int64_t *seg_off, const int32_t *seg_slots,
+                        const float *pos3d_radii_grad, const float *conics_grad,
+                        const float *intensities_grad, const float *loss,
+                        const float *flags, float *send, void *stream) {
+    return halo_pack_grads_impl("gsv_halo_pack_grads", n_own, C, world, rank,
+                                seg_off, seg_slots, pos3d_radii_grad,
+                                conics_grad, intensities_grad, loss, flags, send,
+                                nullptr, stream);
+}
+
+int gsv_halo_pack_grads_peers(int32_t n_own, int32_t C, int32_t world,
+                              int32_t rank, const int64_t *seg_off,
+                              const int32_t *seg_slots,
+                              const float *pos3d_radii_grad,
+                              const float *conics_grad,
+                              const float *intensities_grad, const float *loss,
+                              const float *flags, const int64_t *seg_dst,
+                              void *stream) {
+    return halo_pack_grads_impl("gsv_halo_pack_grads_peers", n_own, C, world,
+                                rank, seg_off, seg_slots, pos3d_radii_grad,
+                                conics_grad, intensities_grad, loss, flags,
+                                nullptr, seg_dst, stream);
 }
 
 int gsv_halo_accumulate(int32_t n, int32_t C, int32_t world,
@@ -958,3 +1038,19 @@ int gsv_tv3d(int32_t channels, const int32_t dhw[3], const float *vol,
 }
 
 }  // extern "C"
+
+extern "C" int gsv_peer_barrier(int32_t world, int32_t rank, const int64_t *sig_ptrs,
+                                int32_t *epoch, void *stream) {
+    const char *fn = "gsv_peer_barrier";
+    GSV_REQUIRE(world >= 1 && world <= gsv::kHaloMaxRanks && rank >= 0 &&
+                    rank < world && sig_ptrs && epoch,
+                GSV_ERR_INVALID_ARGUMENT, "%s: bad ranks or null pointer", fn);
+    for (int d = 0; d < world; ++d)
+        GSV_REQUIRE(sig_ptrs[d] != 0 && (sig_ptrs[d] & 3) == 0,
+                    GSV_ERR_INVALID_ARGUMENT, "%s: bad signal address of rank %d",
+                    fn, d);
+    return cuda_status(gsv::launch_peer_barrier(
+                           world, rank, reinterpret_cast<const long long *>(sig_ptrs),
+                           epoch, as_stream(stream)),
+                       fn);
+}

@@ -97,6 +97,10 @@ struct HaloPeers {
     long long off[kHaloMaxRanks];                // segment start (records)
     int cap[kHaloMaxRanks];                      // slots per segment
     long long loff[kHaloMaxRanks];               // local index of slot 0 - n_own
+    // where this rank's segment for peer d starts (its header record): in a
+    // local send buffer, or directly in peer d's receive buffer (its device
+    // memory, reached over NVLink); the packing kernels write there
+    float *dst[kHaloMaxRanks];
 };
 
 // 2^x on the special-function unit (MUFU.EX2), flush-to-zero.

@@ -72,7 +72,7 @@ halo_pack_kernel(int n, int C, const float4 *__restrict__ pr,
                  const float2 *__restrict__ cq, const float *__restrict__ inten,
                  const int *__restrict__ tmin, const int *__restrict__ tmax,
                  HaloPeers P, const int *__restrict__ block_base,
-                 float *__restrict__ send, int *__restrict__ slot_map) {
+                 int *__restrict__ slot_map) {
     __shared__ int warp_base[kHaloScan / 32];
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -103,7 +103,7 @@ halo_pack_kernel(int n, int C, const float4 *__restrict__ pr,
                               warp_base[wid] + __popc(m & ((1u << lane) - 1u));
                 if (s < P.cap[d]) {
                     slot = s;
-                    float *r = send + (P.off[d] + 1 + s) * kHaloRec;
+                    float *r = P.dst[d] + (1 + s) * kHaloRec;
                     const float4 p = pr[i];
                     reinterpret_cast<float4 *>(r)[0] = p;
                     const float2 a = cq[3 * i], b = cq[3 * i + 1], c = cq[3 * i + 2];
@@ -128,13 +128,12 @@ halo_pack_kernel(int n, int C, const float4 *__restrict__ pr,
 // Header record of each destination segment: [count (int bits), overflow];
 // counts_out[d] (optional) = unclamped number of Gaussians for rank d
 __global__ void halo_header_kernel(HaloPeers P, const long long *__restrict__ totals,
-                                   float *__restrict__ send,
                                    long long *__restrict__ counts_out) {
     const int d = threadIdx.x;
     if (d >= P.world) return;
     if (counts_out) counts_out[d] = d == P.rank ? 0 : totals[d];
     if (d == P.rank) return;
-    float *h = send + P.off[d] * kHaloRec;
+    float *h = P.dst[d];
     const long long t = totals[d];
     h[0] = __int_as_float((int)(t < P.cap[d] ? t : (long long)P.cap[d]));
     h[1] = t > P.cap[d] ? 1.f : 0.f;
@@ -199,11 +198,10 @@ __global__ void __launch_bounds__(256)
 halo_pack_grads_kernel(int n_own, int C, HaloPeers R, long long total_slots,
                        const float4 *__restrict__ gp,
                        const float2 *__restrict__ gc, const float *__restrict__ gi,
-                       const float *__restrict__ loss, const float *__restrict__ flags,
-                       float *__restrict__ send) {
+                       const float *__restrict__ loss, const float *__restrict__ flags) {
     const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (g < R.world && g != R.rank) {
-        float *h = send + R.off[g] * kHaloGrad;
+        float *h = R.dst[g];
         h[0] = loss[0];
         h[1] = fmaxf(flags[0], flags[1]);
     }
@@ -213,7 +211,7 @@ halo_pack_grads_kernel(int n_own, int C, HaloPeers R, long long total_slots,
         if (k != R.rank && R.cap[k] > 0 && g >= R.loff[k]) s = k;
     const int slot = (int)(g - R.loff[s]);
     const long long li = n_own + g;
-    float *r = send + (R.off[s] + 1 + slot) * kHaloGrad;
+    float *r = R.dst[s] + (1 + slot) * kHaloGrad;
     reinterpret_cast<float4 *>(r)[0] = gp[li];
     const float2 a = gc[3 * li], b = gc[3 * li + 1], c = gc[3 * li + 2];
     reinterpret_cast<float4 *>(r)[1] = make_float4(a.x, a.y, b.x, b.y);
@@ -276,7 +274,78 @@ halo_accumulate_kernel(int n, int C, HaloPeers P, const int *__restrict__ slot_m
     for (int k = 0; k < C; ++k) gi[(size_t)i * C + k] = I[k];
 }
 
+// Device barrier across the ranks' GPUs, for the direct-write exchange.
+// Every rank holds a signal array of `world` ints in memory its peers can
+// write (symmetric memory over NVLink); sig[d] is rank d's device address of
+// its array. A call takes the next epoch from the rank's own counter, stores
+// it (release, system scope) into slot `rank` of every peer's array, and
+// waits until every peer's slot in its own array has reached it (acquire
+// loads). Epochs only grow, so the barrier needs no reset and can be
+// replayed inside a CUDA graph. The kernels before it on the stream (the
+// packing kernels' stores into the peers' buffers) have completed when it
+// starts; the release store orders them before the signal. Each wait is
+// bounded: on timeout the kernel records an error in g_peer_error and
+// returns.
+__device__ int g_peer_error = 0;
+
+struct PeerSig {
+    int *sig[kHaloMaxRanks];
+};
+
+constexpr long long kPeerSpinLimit = 1LL << 22;  // polls of ~0.5 us
+
+__global__ void __launch_bounds__(kHaloMaxRanks)
+peer_barrier_kernel(int world, int rank, PeerSig S, int *__restrict__ epoch) {
+    __shared__ int e;
+    if (threadIdx.x == 0) {
+        e = *epoch + 1;
+        *epoch = e;
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d < world && d != rank) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(S.sig[d] + rank),
+                     "r"(e)
+                     : "memory");
+        const int *mine = S.sig[rank] + d;
+        int v = 0;
+        for (long long it = 0; it < kPeerSpinLimit; ++it) {
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine)
+                         : "memory");
+            if (v >= e) break;
+            __nanosleep(500);
+        }
+        if (v < e) atomicExch(&g_peer_error, 1);
+    }
+    __syncthreads();
+    __threadfence_system();
+}
+
 }  // namespace
+
+cudaError_t launch_peer_barrier(int world, int rank, const long long *sig_ptrs,
+                                int *epoch, cudaStream_t stream) {
+    PeerSig S;
+    for (int d = 0; d < kHaloMaxRanks; ++d)
+        S.sig[d] = d < world ? reinterpret_cast<int *>(
+                                   static_cast<uintptr_t>(sig_ptrs[d]))
+                             : nullptr;
+    peer_barrier_kernel<<<1, kHaloMaxRanks, 0, stream>>>(world, rank, S, epoch);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+int peer_error_flag(bool clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_peer_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear && v) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_peer_error, &zero, sizeof(int)) != cudaSuccess)
+            return -1;
+    }
+    return v;
+}
 
 size_t halo_workspace_bytes(int n, int world) {
     const size_t nb = (size_t)((n + kHaloScan - 1) / kHaloScan);
@@ -286,7 +355,7 @@ size_t halo_workspace_bytes(int n, int world) {
 
 cudaError_t launch_halo_pack(int n, int C, const float *pr, const float *cq,
                              const float *inten, const int *tmin,
-                             const int *tmax, const HaloPeers &P, float *send,
+                             const int *tmax, const HaloPeers &P,
                              int *slot_map, long long *counts_out, void *ws,
                              cudaStream_t stream) {
     const int nb = (n + kHaloScan - 1) / kHaloScan;
@@ -303,9 +372,8 @@ cudaError_t launch_halo_pack(int n, int C, const float *pr, const float *cq,
         halo_pack_kernel<<<nb, kHaloScan, 0, stream>>>(
             n, C, reinterpret_cast<const float4 *>(pr),
             reinterpret_cast<const float2 *>(cq), inten, tmin, tmax, P, counts,
-            send, slot_map);
-    halo_header_kernel<<<1, kHaloMaxRanks, 0, stream>>>(P, totals, send,
-                                                        counts_out);
+            slot_map);
+    halo_header_kernel<<<1, kHaloMaxRanks, 0, stream>>>(P, totals, counts_out);
     count_launches(nb > 0 ? 3 : 2);
     return cudaGetLastError();
 }
@@ -327,12 +395,12 @@ cudaError_t launch_halo_pack_grads(int n_own, int C, const HaloPeers &R,
                                    long long total_slots, const float *gp,
                                    const float *gc, const float *gi,
                                    const float *loss, const float *flags,
-                                   float *send, cudaStream_t stream) {
+                                   cudaStream_t stream) {
     const long long threads = std::max<long long>(total_slots, R.world);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     halo_pack_grads_kernel<<<blocks, 256, 0, stream>>>(
         n_own, C, R, total_slots, reinterpret_cast<const float4 *>(gp),
-        reinterpret_cast<const float2 *>(gc), gi, loss, flags, send);
+        reinterpret_cast<const float2 *>(gc), gi, loss, flags);
     count_launches(1);
     return cudaGetLastError();
 }

@@ -83,6 +83,58 @@ class NcclComm:
                                group=self.group)
 
 
+class SymmComm(NcclComm):
+    """The step's exchanges as direct writes into the peers' receive buffers
+    (torch symmetric memory over NVLink, plain stores from this library's
+    packing kernels) followed by this library's device barrier across the
+    ranks (gsv_peer_barrier, on a small symmetric signal array); the receive
+    buffers are symmetric allocations of equal size on every rank. Nothing
+    runs on the host between the stages, so a whole step can be one CUDA
+    graph. NVLink multicast is not used (TORCH_SYMM_MEM_DISABLE_MULTICAST)."""
+
+    graph_safe = True  # device_barrier is a graph-capturable kernel
+
+    def __init__(self, group=None):
+        super().__init__(group)
+        import os
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        self._handles = {}
+        self._sig = None
+
+    def _signals(self, device):
+        if self._sig is None:
+            import torch.distributed._symmetric_memory as symm_mem
+            sig = symm_mem.empty(self.world, dtype=torch.int32, device=device)
+            sig.zero_()
+            torch.cuda.current_stream(device).synchronize()
+            h = symm_mem.rendezvous(sig, self.group if self.group is not None
+                                    else dist.group.WORLD)
+            self._sig = (sig, h, _i64([int(p) for p in h.buffer_ptrs]),
+                         torch.zeros((1,), dtype=torch.int32, device=device))
+        return self._sig
+
+    def symmetric(self, key: str, numel: int, device) -> Tuple[torch.Tensor, List[int]]:
+        """A float32 buffer of numel elements on every rank (collective), and
+        the device addresses of every rank's copy."""
+        import torch.distributed._symmetric_memory as symm_mem
+        t = symm_mem.empty(numel, dtype=torch.float32, device=device)
+        t.zero_()
+        # zeroed before any peer can write into it: the rendezvous below
+        # returns on no rank before every rank has entered it
+        torch.cuda.current_stream(device).synchronize()
+        h = symm_mem.rendezvous(t, self.group if self.group is not None
+                                else dist.group.WORLD)
+        self._handles[key] = h
+        return t, [int(p) for p in h.buffer_ptrs]
+
+    def device_barrier(self, key: str) -> None:
+        """Every rank's preceding writes into the buffers are visible to
+        every rank after this point of its stream (one barrier kernel)."""
+        sig, _, ptrs, epoch = self._signals(torch.device("cuda", torch.cuda.current_device()))
+        check(lib.gsv_peer_barrier(self.world, self.rank, ptrs, epoch.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream))
+
+
 def segments(slots: Sequence[int], rank: int, rec: int) -> Tuple[List[int], List[int], int]:
     """Layout of an exchange buffer with one segment per peer: a header
     record plus slots[peer] record slots (none for the rank itself). Returns
@@ -124,8 +176,11 @@ class HaloL1Step:
     def __init__(self, pos3d, scale3d, quat, intensities, vol_size_voxel,
                  vol_size_world, vol_center_pos, target, comm=None,
                  denom: Optional[float] = None, headroom: float = 1.25,
-                 use_graph: bool = True):
-        self.comm = comm or NcclComm()
+                 use_graph: bool = True, exchange: str = "nccl"):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.comm = comm or (SymmComm() if exchange == "p2p" else NcclComm())
+        self.p2p = exchange == "p2p"
         self.world, self.rank = self.comm.world, self.comm.rank
         if not 1 <= self.world <= 64:
             raise ValueError("1..64 ranks supported")
@@ -185,6 +240,7 @@ class HaloL1Step:
         self._graphs = None
         self.caps_out = [0] * self.world   # slots this rank sends to each peer
         self.caps_in = [0] * self.world    # slots each peer sends to this rank
+        self.caps_matrix = [[0] * self.world for _ in range(self.world)]
         self.n_loc = -1
         self.pair_cap = 0
         self.ids = None
@@ -216,10 +272,34 @@ class HaloL1Step:
         self.c1_recv, self.o1_recv, r1r = segments(self.caps_in, self.rank, REC)
         self.c2_send, self.o2_send, r2s = segments(self.caps_in, self.rank, GREC)
         self.c2_recv, self.o2_recv, r2r = segments(self.caps_out, self.rank, GREC)
-        self.send1 = torch.zeros((max(r1s, 1) * REC,), **f32)
-        self.recv1 = torch.zeros((max(r1r, 1) * REC,), **f32)
-        self.send2 = torch.zeros((max(r2s, 1) * GREC,), **f32)
-        self.recv2 = torch.zeros((max(r2r, 1) * GREC,), **f32)
+        if self.p2p and self.world > 1:
+            # symmetric receive buffers, equal sizes on every rank (the
+            # largest any rank needs, from the all-gathered capacities);
+            # each rank's packing kernels write its segments straight into
+            # them (seg_dst), so there are no send buffers
+            M = self.caps_matrix
+            col = lambda d: [M[s][d] for s in range(self.world)]  # noqa: E731
+            n1 = max(segments(col(d), d, REC)[2] for d in range(self.world))
+            n2 = max(segments(M[d], d, GREC)[2] for d in range(self.world))
+            self.recv1, p1 = self.comm.symmetric("recv1", max(n1, 1) * REC, dev)
+            self.recv2, p2 = self.comm.symmetric("recv2", max(n2, 1) * GREC, dev)
+            dst1 = [0] * self.world
+            dst2 = [0] * self.world
+            for d in range(self.world):
+                if d == self.rank:
+                    continue
+                # this rank's segment in d's record buffer (laid out by the
+                # slots every rank sends to d) and in d's gradient buffer
+                # (laid out by the slots d sends to every rank)
+                dst1[d] = p1[d] + 4 * REC * segments(col(d), d, REC)[1][self.rank]
+                dst2[d] = p2[d] + 4 * GREC * segments(M[d], d, GREC)[1][self.rank]
+            self._dst1, self._dst2 = _i64(dst1), _i64(dst2)
+            self.send1 = self.send2 = None
+        else:
+            self.send1 = torch.zeros((max(r1s, 1) * REC,), **f32)
+            self.recv1 = torch.zeros((max(r1r, 1) * REC,), **f32)
+            self.send2 = torch.zeros((max(r2s, 1) * GREC,), **f32)
+            self.recv2 = torch.zeros((max(r2r, 1) * GREC,), **f32)
         self._o1s, self._o1r = _i64(self.o1_send), _i64(self.o1_recv)
         self._o2s, self._o2r = _i64(self.o2_send), _i64(self.o2_recv)
         self._cap_out, self._cap_in = _i32(self.caps_out), _i32(self.caps_in)
@@ -242,7 +322,10 @@ class HaloL1Step:
                   if self.world > 1 else [caps])
         caps_out = list(matrix[self.rank])
         caps_in = [matrix[s][self.rank] for s in range(self.world)]
-        if caps_out != self.caps_out or caps_in != self.caps_in:
+        matrix = [list(r) for r in matrix]
+        if matrix != self.caps_matrix:
+            # (the same decision on every rank: the matrix is all-gathered)
+            self.caps_matrix = matrix
             self.caps_out, self.caps_in = caps_out, caps_in
             self._alloc_local()
 
@@ -290,13 +373,16 @@ class HaloL1Step:
             self.inten[:self.n].copy_(inten.view(self.n, self.C))
 
     def _pack(self) -> None:
-        check(lib.gsv_halo_pack(
-            self.n, self.C, self.pr.data_ptr(), self.cq.data_ptr(),
-            self.inten.data_ptr(), self.tmin.data_ptr(), self.tmax.data_ptr(),
-            self.world, self.rank, self._slab_tz, _i64(self.o1_send),
-            _i32(self.caps_out), self.send1.data_ptr(), self.slot_map.data_ptr(),
-            self.halo_counts.data_ptr(), self.halo_ws.data_ptr(),
-            self.halo_ws.numel(), self._stream()))
+        args = (self.n, self.C, self.pr.data_ptr(), self.cq.data_ptr(),
+                self.inten.data_ptr(), self.tmin.data_ptr(), self.tmax.data_ptr(),
+                self.world, self.rank, self._slab_tz, _i64(self.o1_send),
+                _i32(self.caps_out))
+        tail = (self.slot_map.data_ptr(), self.halo_counts.data_ptr(),
+                self.halo_ws.data_ptr(), self.halo_ws.numel(), self._stream())
+        if self.send1 is None:
+            check(lib.gsv_halo_pack_peers(*args, self._dst1, *tail))
+        else:
+            check(lib.gsv_halo_pack(*args, self.send1.data_ptr(), *tail))
 
     def _unpack(self) -> None:
         self.flags.zero_()
@@ -329,11 +415,14 @@ class HaloL1Step:
             _C._ptr(self.target), self.grad_loss.data_ptr(), self.denom,
             self.gp.data_ptr(), self.gc.data_ptr(), self.gi.data_ptr(),
             self.ws.data_ptr(), self.ws.numel(), self._stream()))
-        check(lib.gsv_halo_pack_grads(
-            self.n, self.C, self.world, self.rank, self._o2s, self._cap_in,
-            self.gp.data_ptr(), self.gc.data_ptr(), self.gi.data_ptr(),
-            self.loss.data_ptr(), self.flags.data_ptr(), self.send2.data_ptr(),
-            self._stream()))
+        args = (self.n, self.C, self.world, self.rank, self._o2s, self._cap_in,
+                self.gp.data_ptr(), self.gc.data_ptr(), self.gi.data_ptr(),
+                self.loss.data_ptr(), self.flags.data_ptr())
+        if self.send2 is None:
+            check(lib.gsv_halo_pack_grads_peers(*args, self._dst2, self._stream()))
+        else:
+            check(lib.gsv_halo_pack_grads(*args, self.send2.data_ptr(),
+                                          self._stream()))
 
     def stage_c(self) -> None:
         check(lib.gsv_halo_accumulate(
@@ -352,26 +441,45 @@ class HaloL1Step:
         self._host.copy_(self.out, non_blocking=True)
 
     def exchange_records(self) -> None:
-        if self.world > 1:
+        if self.world == 1:
+            return
+        if self.send1 is None:  # written in place by the peers' packing
+            self.comm.device_barrier("recv1")
+        else:
             self.comm.all_to_all(self.send1, self.c1_send, self.recv1,
                                  self.c1_recv)
 
     def exchange_grads(self) -> None:
-        if self.world > 1:
+        if self.world == 1:
+            return
+        if self.send2 is None:
+            self.comm.device_barrier("recv2")
+        else:
             self.comm.all_to_all(self.send2, self.c2_send, self.recv2,
                                  self.c2_recv)
 
     # ---------------------------------------------------------------- run
 
-    def _capture(self) -> None:
-        before = lib.gsv_launch_count()
+    def _whole_step(self) -> None:
         self.stage_a()
         self.exchange_records()
         self.stage_b()
         self.exchange_grads()
         self.stage_c()
+
+    def _capture(self) -> None:
+        before = lib.gsv_launch_count()
+        self._whole_step()
         self.launches_per_step = int(lib.gsv_launch_count() - before)
         torch.cuda.current_stream(self.device).synchronize()
+        if self.world == 1 or getattr(self.comm, "graph_safe", False):
+            # exchanges by device barriers (or none): the whole step is one
+            # graph
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._whole_step()
+            self._graphs = [g]
+            return
         graphs = []
         for stage in (self.stage_a, self.stage_b, self.stage_c):
             g = torch.cuda.CUDAGraph()
@@ -392,6 +500,9 @@ class HaloL1Step:
             return
         if self._graphs is None:
             self._capture()
+        if len(self._graphs) == 1:
+            self._graphs[0].replay()
+            return
         ga, gb, gc = self._graphs
         ga.replay()
         self.exchange_records()

@@ -353,10 +353,11 @@ GSV_API int gsv_tv3d(int32_t channels, const int32_t dhw[3], const float *vol,
 GSV_API int gsv_set_tensor_core_backward(int32_t enable);
 
 /*
- * Device error flag of this library's kernels on the current device: 1 after
- * a tensor-core backward launch gave up waiting on one of its internal
- * barriers (its results are then invalid), else 0. clear != 0 resets it.
- * Synchronises with the device. No reference counterpart.
+ * Device error flags of this library's kernels on the current device, as
+ * bits: 1 after a tensor-core backward launch gave up waiting on one of its
+ * internal barriers, 2 after a gsv_peer_barrier gave up waiting for a peer
+ * (results of those launches are invalid); 0 if none. clear != 0 resets
+ * them. Synchronises with the device. No reference counterpart.
  */
 GSV_API int gsv_device_error(int32_t *flag_out, int32_t clear);
 
@@ -440,6 +441,53 @@ GSV_API int gsv_halo_pack_grads(int32_t n_own, int32_t channels, int32_t world,
                                 const float *intensities_grad,
                                 const float *loss, const float *flags,
                                 float *send, void *stream);
+
+/*
+ * Device barrier across `world` ranks (one GPU each) on `stream`, for the
+ * direct-write halo exchange: sig_ptrs[d] is the device address of rank d's
+ * signal array of `world` int32 (zero-initialised memory that every rank
+ * can write, e.g. a symmetric-memory buffer over NVLink), `epoch` a device
+ * int32 of this rank (initially 0) that the call advances. After the call,
+ * on every rank's stream, all writes of the kernels before every rank's call
+ * are visible. Graph-capturable (the epochs only grow); every rank must make
+ * the same sequence of calls. Waits are bounded (about two seconds per
+ * peer): on timeout the kernel sets bit 2 of gsv_device_error and returns.
+ * No reference counterpart.
+ */
+GSV_API int gsv_peer_barrier(int32_t world, int32_t rank, const int64_t *sig_ptrs,
+                             int32_t *epoch, void *stream);
+
+/*
+ * gsv_halo_pack_peers / gsv_halo_pack_grads_peers: as gsv_halo_pack /
+ * gsv_halo_pack_grads, but each segment is written straight into the
+ * destination rank's receive buffer instead of a local send buffer:
+ * seg_dst[d] (d != rank) is the device address, 16-byte aligned, where this
+ * rank's segment starts in rank d's receive buffer (memory of another GPU
+ * reached over NVLink, e.g. a peer's symmetric-memory buffer; plain stores,
+ * no multicast). The caller makes every rank's writes visible to their
+ * receivers (a device barrier across the ranks) before the unpack /
+ * accumulate. seg_off and seg_slots describe the segments as for the other
+ * calls. No reference counterpart.
+ */
+GSV_API int gsv_halo_pack_peers(int32_t num_gaussians, int32_t channels,
+                                const float *pos3d_radii, const float *conics,
+                                const float *intensities, const int32_t *tile_min,
+                                const int32_t *tile_max, int32_t world,
+                                int32_t rank, const int32_t *slab_tz,
+                                const int64_t *seg_off, const int32_t *seg_slots,
+                                const int64_t *seg_dst, int32_t *slot_map,
+                                int64_t *counts_out, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
+GSV_API int gsv_halo_pack_grads_peers(int32_t n_own, int32_t channels,
+                                      int32_t world, int32_t rank,
+                                      const int64_t *seg_off,
+                                      const int32_t *seg_slots,
+                                      const float *pos3d_radii_grad,
+                                      const float *conics_grad,
+                                      const float *intensities_grad,
+                                      const float *loss, const float *flags,
+                                      const int64_t *seg_dst, void *stream);
 
 GSV_API int gsv_halo_accumulate(int32_t num_gaussians, int32_t channels,
                                 int32_t world, int32_t rank,

@@ -1,5 +1,6 @@
 """Run by tests/test_gpu_multi.py under torch.distributed.run (one process
-per GPU, NCCL): the owner-sharded step (halo.HaloL1Step) and the replicated
+per GPU, NCCL): the owner-sharded step (halo.HaloL1Step, with NCCL
+all-to-alls and with direct peer writes + device barriers) and the replicated
 step (step.FusedL1Step with a process group) against the single-GPU step
 over the whole volume, computed on every rank. Writes one JSON result per
 rank into the directory given as argv[1]."""
@@ -51,6 +52,14 @@ def main():
     res["halo_slots_in"] = sum(halo.caps_in)
     ii = torch.from_numpy(idx).cuda()
     res["halo_grad_err"] = [rel_err(p.grad, g[ii]) for p, g in zip(own, ref_grads)]
+    # owner-sharded, exchanges as direct writes into the peers' symmetric
+    # receive buffers + device barriers
+    own2 = [dev(a[idx]) for a in arrs]
+    halo2 = HaloL1Step(*own2, cfg.vol, cfg.world, cfg.center, slab_target,
+                       exchange="p2p")
+    res["p2p_loss"] = [halo2.run() for _ in range(3)]
+    res["p2p_grad_err"] = [rel_err(p.grad, g[ii]) for p, g in zip(own2, ref_grads)]
+    del halo2
     # replicated
     rep_params = [dev(a) for a in arrs]
     rep = FusedL1Step(*rep_params, cfg.vol, cfg.world, cfg.center, slab_target,

@@ -26,6 +26,7 @@ class _Shared:
         self.world = world
         self.barrier = threading.Barrier(world, timeout=120)
         self.slots = [None] * world
+        self.keep = {}  # symmetric buffers of all ranks, kept alive
 
 
 class ThreadComm:
@@ -41,6 +42,23 @@ class ThreadComm:
         out = [list(v) for v in self.s.slots]
         self.s.barrier.wait()
         return out
+
+    def symmetric(self, key, numel, device):
+        """p2p exchange: a buffer per rank, every rank's address known to all
+        (on one GPU the 'peer' buffers are other threads' allocations)."""
+        t = torch.zeros((numel,), dtype=torch.float32, device=device)
+        torch.cuda.current_stream().synchronize()
+        self.s.barrier.wait()
+        self.s.slots[self.rank] = t
+        self.s.barrier.wait()
+        ptrs = [int(b.data_ptr()) for b in self.s.slots]
+        self.s.keep.setdefault(key, {})[self.rank] = t
+        self.s.barrier.wait()
+        return t, ptrs
+
+    def device_barrier(self, key):
+        torch.cuda.current_stream().synchronize()
+        self.s.barrier.wait()
 
     def all_to_all(self, send, send_counts, recv, recv_counts):
         torch.cuda.current_stream().synchronize()
@@ -71,7 +89,8 @@ def close(got, want, rtol, atol_rel, name):
     assert not bad.any(), f"{name}: {bad.sum()} of {bad.size} out of tolerance"
 
 
-def _run_ranks(cfg, world, arrs, target_full, shrink=None, steps=2):
+def _run_ranks(cfg, world, arrs, target_full, shrink=None, steps=2,
+               exchange="nccl"):
     from gs_voxelizer_b200.halo import HaloL1Step, owner_of
     from gs_voxelizer_b200.slab import slab_bounds
     owners = owner_of(arrs[0], cfg.vol, cfg.world, cfg.center, world)
@@ -86,11 +105,14 @@ def _run_ranks(cfg, world, arrs, target_full, shrink=None, steps=2):
             tz0, tz1 = slab_bounds(cfg.vol, world, rank)
             target = target_full[8 * tz0:min(cfg.vol[0], 8 * tz1)].contiguous()
             step = HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
-                              comm=ThreadComm(shared, rank), use_graph=False)
+                              comm=ThreadComm(shared, rank), use_graph=False,
+                              exchange=exchange)
             if shrink is not None:  # every rank: `shrink` slots per peer,
                 # too few, so the halo overflows
                 step.caps_out = [0 if d == rank else shrink for d in range(world)]
                 step.caps_in = [0 if d == rank else shrink for d in range(world)]
+                step.caps_matrix = [[0 if a == b else shrink for b in range(world)]
+                                    for a in range(world)]
                 step._alloc_local()
                 step._size_pairs(step.pair_cap)
             losses = [step.run() for _ in range(steps)]
@@ -119,8 +141,9 @@ def _reference(cfg, arrs, target):
     return loss, [p.grad.clone() for p in params], step.volume.clone()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
 @pytest.mark.parametrize("world,channels", [(2, 1), (3, 1), (2, 3)])
-def test_halo_step_matches_single_gpu(world, channels):
+def test_halo_step_matches_single_gpu(world, channels, exchange):
     from gs_voxelizer_b200.workloads import phantom
     from gs_voxelizer_b200.slab import slab_bounds
     cfg = K.small_config(vol=(72, 40, 48), n=4000, seed=80, channels=channels,
@@ -128,7 +151,7 @@ def test_halo_step_matches_single_gpu(world, channels):
     arrs = list(K.inputs(cfg))
     target = phantom(cfg, device="cuda")
     want_loss, want_grads, want_vol = _reference(cfg, arrs, target)
-    res = _run_ranks(cfg, world, arrs, target)
+    res = _run_ranks(cfg, world, arrs, target, exchange=exchange)
     halo = sum(sum(r["step"].caps_in) for r in res)
     assert halo > 0  # Gaussians do cross the slab boundaries
     for r in res:
@@ -148,8 +171,9 @@ def test_halo_step_matches_single_gpu(world, channels):
         assert bool((err <= 1e-5 * ref.double().abs() + 1e-6).all()), float(err.max())
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
 @pytest.mark.parametrize("slots", [1, 0])
-def test_halo_overflow_regrows_on_every_rank(slots):
+def test_halo_overflow_regrows_on_every_rank(slots, exchange):
     """Too few halo slots: one per peer, or none at all (then no record
     slot exists and the overflow is known only from the senders' headers)."""
     from gs_voxelizer_b200.workloads import phantom
@@ -157,7 +181,8 @@ def test_halo_overflow_regrows_on_every_rank(slots):
     arrs = list(K.inputs(cfg))
     target = phantom(cfg, device="cuda")
     want_loss, want_grads, _ = _reference(cfg, arrs, target)
-    res = _run_ranks(cfg, 2, arrs, target, shrink=slots, steps=1)
+    res = _run_ranks(cfg, 2, arrs, target, shrink=slots, steps=1,
+                     exchange=exchange)
     for r in res:
         assert r["step"].regrows == 1
         assert r["losses"][0] == pytest.approx(want_loss, rel=1e-5)

@@ -37,7 +37,7 @@ def test_halo_and_replicated_steps_on_two_gpus(tmp_path):
         res = json.load(open(tmp_path / f"rank{rank}.json"))
         want = res["ref_loss"]
         assert res["halo_slots_in"] > 0
-        for loss in res["halo_loss"] + res["rep_loss"]:
+        for loss in res["halo_loss"] + res["p2p_loss"] + res["rep_loss"]:
             assert loss == pytest.approx(want, rel=1e-5), res
-        for e in res["halo_grad_err"] + res["rep_grad_err"]:
+        for e in res["halo_grad_err"] + res["p2p_grad_err"] + res["rep_grad_err"]:
             assert e < 1e-4, res

@@ -262,63 +262,96 @@ ssim_bwd_kernel(int D, int H, int W, int zchunks, const float *__restrict__ img1
         });
 }
 
-// TV: value partials per block and the gradient (grad_out scaled). One
-// thread per voxel: block (32, 8) over (x, y), grid z = D * channels.
+// TV: value partials per block and the gradient (grad_out scaled). Block
+// (32, 8) over (x, y); each thread marches down a run of kTvZ z-planes of
+// its column, so the differences at v - e_z are the previous plane's and
+// every value of the next plane it needs is loaded once: per voxel 3 loads
+// for the value, 7 with the gradient. Grid z = runs * channels.
+constexpr int kTvZ = 8;
+
+template <bool ISO>
+__device__ __forceinline__ float tv_term(float dx, float dy, float dz, float eps) {
+    return ISO ? sqrtf(dx * dx + dy * dy + dz * dz + eps)
+               : fabsf(dx) + fabsf(dy) + fabsf(dz);
+}
+
+__device__ __forceinline__ float sgnf(float v) { return (float)((v > 0.f) - (v < 0.f)); }
+
 template <bool ISO>
 __global__ void __launch_bounds__(256)
-tv_kernel(int D, int H, int W, const float *__restrict__ x, float eps,
+tv_kernel(int D, int H, int W, int runs, const float *__restrict__ x, float eps,
           float inv_n, const float *__restrict__ grad_out,
           float *__restrict__ grad, float *__restrict__ part) {
     __shared__ float red[8];
     const int xx = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * 8 + threadIdx.y;
-    const int z = blockIdx.z % D, ch = blockIdx.z / D;
+    const int run = blockIdx.z % runs, ch = blockIdx.z / runs;
+    const int z0 = run * kTvZ, z1 = min(D, z0 + kTvZ);
     const size_t plane = (size_t)H * W;
     float lsum = 0.f;
     if (xx < W && y < H) {
         const float *xc = x + (size_t)ch * plane * D;
-        const size_t i = (size_t)z * plane + (size_t)y * W + xx;
-        // forward differences at voxel j = (zz, yy, xw), 0 across the far edge
-        auto diffs = [&](size_t j, int zz, int yy, int xw, float &dx, float &dy,
-                         float &dz) {
-            const float cj = __ldg(xc + j);
-            dx = xw + 1 < W ? __ldg(xc + j + 1) - cj : 0.f;
-            dy = yy + 1 < H ? __ldg(xc + j + W) - cj : 0.f;
-            dz = zz + 1 < D ? __ldg(xc + j + plane) - cj : 0.f;
+        const size_t col = (size_t)y * W + xx;
+        const bool hx = xx + 1 < W, hy = y + 1 < H, bx = xx > 0, by = y > 0;
+        const float g = grad ? __ldg(grad_out) * inv_n : 0.f;
+        // value at (z, column + off), 0 outside [0, D)
+        auto at = [&](int z, long long off) {
+            return (z >= 0 && z < D) ? __ldg(xc + (size_t)z * plane + col + off) : 0.f;
         };
-        auto sgn = [](float v) { return (float)((v > 0.f) - (v < 0.f)); };
-        float dx, dy, dz;
-        diffs(i, z, y, xx, dx, dy, dz);
-        float t, gr;
-        if (ISO) {
-            t = sqrtf(dx * dx + dy * dy + dz * dz + eps);
-            gr = -(dx + dy + dz) / t;
-        } else {
-            t = fabsf(dx) + fabsf(dy) + fabsf(dz);
-            gr = -(sgn(dx) + sgn(dy) + sgn(dz));
+        float c = at(z0, 0);                     // x(v)
+        float a = bx ? at(z0, -1) : 0.f;         // x(v - ex)
+        float b = by ? at(z0, -W) : 0.f;         // x(v - ey)
+        // the voxel behind in z: its differences dz and its term
+        float pdz = 0.f, pt = 1.f;
+        if (grad && z0 > 0) {
+            const float pc = at(z0 - 1, 0);
+            const float pdx = hx ? at(z0 - 1, 1) - pc : 0.f;
+            const float pdy = hy ? at(z0 - 1, W) - pc : 0.f;
+            pdz = c - pc;
+            pt = tv_term<ISO>(pdx, pdy, pdz, eps);
         }
-        lsum = t;
-        if (grad) {
-            // the terms of the three neighbours behind v that contain x(v)
-            float ex, ey, ez;
-            if (xx > 0) {
-                diffs(i - 1, z, y, xx - 1, ex, ey, ez);
-                gr += ISO ? ex / sqrtf(ex * ex + ey * ey + ez * ez + eps) : sgn(ex);
+        for (int z = z0; z < z1; ++z) {
+            const bool hz = z + 1 < D;
+            const float cz = hz ? at(z + 1, 0) : 0.f;  // next plane's c
+            const float dx = hx ? at(z, 1) - c : 0.f;
+            const float dy = hy ? at(z, W) - c : 0.f;
+            const float dz = hz ? cz - c : 0.f;
+            const float t = tv_term<ISO>(dx, dy, dz, eps);
+            lsum += t;
+            float az = 0.f, bz = 0.f;
+            if (grad) {
+                float gr = ISO ? -(dx + dy + dz) / t : -(sgnf(dx) + sgnf(dy) + sgnf(dz));
+                if (bx) {  // term of v - ex: dx(v - ex) = x(v) - x(v - ex)
+                    az = hz ? at(z + 1, -1) : 0.f;
+                    const float ex = c - a;
+                    const float ey = hy ? at(z, W - 1) - a : 0.f;
+                    const float ez = hz ? az - a : 0.f;
+                    gr += ISO ? ex / tv_term<true>(ex, ey, ez, eps) : sgnf(ex);
+                }
+                if (by) {  // term of v - ey
+                    bz = hz ? at(z + 1, -W) : 0.f;
+                    const float fx = hx ? at(z, 1 - W) - b : 0.f;
+                    const float fy = c - b;
+                    const float fz = hz ? bz - b : 0.f;
+                    gr += ISO ? fy / tv_term<true>(fx, fy, fz, eps) : sgnf(fy);
+                }
+                if (z > 0)  // term of v - ez (the previous plane's)
+                    gr += ISO ? pdz / pt : sgnf(pdz);
+                grad[(size_t)ch * plane * D + (size_t)z * plane + col] = g * gr;
+                pdz = dz;
+                pt = t;
+            } else {
+                if (bx && hz) az = at(z + 1, -1);
+                if (by && hz) bz = at(z + 1, -W);
             }
-            if (y > 0) {
-                diffs(i - W, z, y - 1, xx, ex, ey, ez);
-                gr += ISO ? ey / sqrtf(ex * ex + ey * ey + ez * ez + eps) : sgn(ey);
-            }
-            if (z > 0) {
-                diffs(i - plane, z - 1, y, xx, ex, ey, ez);
-                gr += ISO ? ez / sqrtf(ex * ex + ey * ey + ez * ez + eps) : sgn(ez);
-            }
-            grad[(size_t)ch * plane * D + i] = __ldg(grad_out) * inv_n * gr;
+            c = cz;
+            a = az;
+            b = bz;
         }
     }
     if (part) {
         const float s = block_sum(lsum, red);
-        const unsigned b = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
-        if (threadIdx.x == 0 && threadIdx.y == 0) part[b] = s;
+        const unsigned blk = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        if (threadIdx.x == 0 && threadIdx.y == 0) part[blk] = s;
     }
 }
 
@@ -407,7 +440,7 @@ cudaError_t launch_ssim_backward(int nch, int D, int H, int W, const float *img1
 
 static dim3 tv_grid(int nch, int D, int H, int W) {
     return dim3((unsigned)((W + 31) / 32), (unsigned)((H + 7) / 8),
-                (unsigned)(D * nch));
+                (unsigned)(((D + kTvZ - 1) / kTvZ) * nch));
 }
 
 size_t tv_workspace_bytes(int nch, int D, int H, int W) {
@@ -423,10 +456,10 @@ cudaError_t launch_tv(int nch, int D, int H, int W, const float *x, int iso,
     float *part = value_out ? static_cast<float *>(ws) : nullptr;
     const float inv_n = (float)(1.0 / (double)total);
     if (iso)
-        tv_kernel<true><<<grid, dim3(32, 8), 0, stream>>>(D, H, W, x, eps, inv_n,
+        tv_kernel<true><<<grid, dim3(32, 8), 0, stream>>>(D, H, W, (D + kTvZ - 1) / kTvZ, x, eps, inv_n,
                                                           grad_out, grad, part);
     else
-        tv_kernel<false><<<grid, dim3(32, 8), 0, stream>>>(D, H, W, x, eps, inv_n,
+        tv_kernel<false><<<grid, dim3(32, 8), 0, stream>>>(D, H, W, (D + kTvZ - 1) / kTvZ, x, eps, inv_n,
                                                            grad_out, grad, part);
     count_launches(1);
     if (value_out) {

@@ -8,18 +8,21 @@ in its slab, see `owner_of`) and a step is
 
   A  project the owned Gaussians; pack the render records of those whose
      tile box reaches another rank's slab (`gsv_halo_pack`)
-  -- all-to-all #1: records to the ranks that need them
+  -- exchange #1: records to the ranks that need them
   B  unpack the received halo after the owned Gaussians; voxelize the slab
      with the fused L1 loss and run the per-Gaussian backward over owned +
      halo; pack the halo's gradients, this rank's loss and overflow flags
-  -- all-to-all #2: gradients back to their owners, plus every rank's header
+  -- exchange #2: gradients back to their owners, plus every rank's header
   C  add the returned gradients to the owned ones in rank order; sum the
      ranks' losses in rank order; projection backward of the owned Gaussians
 
 Traffic and per-rank work scale with the halo, not with the rank count, and
 every rank ends a step with the global loss and a global overflow decision
-without a further collective. A, B and C are CUDA graphs (three launches and
-two NCCL calls per step). Segment capacities (halo slots per rank pair, the
+without a further collective. An exchange is either two NCCL all-to-alls
+(`exchange="nccl"`: A, B and C are three CUDA graphs with the collectives
+between them) or direct writes of the packing kernels into the peers'
+symmetric-memory receive buffers followed by this library's device barrier
+(`exchange="p2p"`: the whole step is one CUDA graph). Segment capacities (halo slots per rank pair, the
 pair buffer of the binning) keep 25 % headroom; an overflow anywhere makes
 every rank re-size (one all-gather of the halo counts) and repeat the step.
 

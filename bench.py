@@ -243,6 +243,7 @@ class Step:
         # Gaussians (losses.voxelize_gaussians_l1); "dropin": the
         # reference-compatible voxelize_gaussians + torch L1
         self.mode = "graph" if impl != "reference" else "dropin"
+        self.per_gaussian = True  # dropin: which backward voxelize_gaussians uses
         self.fstep = None
         self.step_host, self.step_in_bytes = self.host, self.in_bytes
         if impl != "reference":
@@ -274,7 +275,7 @@ class Step:
             pr, cq, tmin, tmax, nt = self.api.optim_to_render(
                 pos, scale, quat, inten, cfg.vol, cfg.world, cfg.center)
             vol = self.api.voxelize_gaussians(pr, cq, inten, cfg.vol, tmin,
-                                              tmax, nt, True)
+                                              tmax, nt, self.per_gaussian)
         else:
             pr, cq, tmin, tmax, nt = self.o2r(pos, scale, quat, inten, cfg.vol,
                                               cfg.world, cfg.center)
@@ -285,7 +286,8 @@ class Step:
                                       plan=self.plan)
                 return loss
             if self.world == 1:
-                vol = self.vox(pr, cq, inten, cfg.vol, tmin, tmax, nt, True)
+                vol = self.vox(pr, cq, inten, cfg.vol, tmin, tmax, nt,
+                               self.per_gaussian)
             else:
                 vol = self.vox_slab(pr, cq, inten, self.plan, tmin, tmax)
         # slab L1 loss normalised by the global voxel count (sums to the
@@ -889,6 +891,19 @@ def main():
         d_ms = max_over_ranks(d_ms, world) / args.steps
         dropin = {"ms_per_step": d_ms, "value": evals_per_step / (d_ms / 1e3),
                   "api": "optim_to_render + voxelize_gaussians + torch l1_loss"}
+    per_voxel = None
+    if world == 1 and not strong:
+        # both arms: the drop-in step with the per-voxel backward
+        # (use_per_gaussian_backward=False, the reference's second path)
+        st.mode, st.per_gaussian = "dropin", False
+        for _ in range(3):
+            st.step()
+        v_ms, _ = time_steps(st.step, max(5, min(args.steps, 30)), flush)
+        v_ms /= max(5, min(args.steps, 30))
+        per_voxel = {"ms_per_step": v_ms, "value": evals_per_step / (v_ms / 1e3),
+                     "api": "optim_to_render + voxelize_gaussians("
+                            "use_per_gaussian_backward=False) + torch l1_loss"}
+        st.per_gaussian = True
     if impl != "reference":
         st.mode = "fused"  # kernel timing below runs the eager launches
 
@@ -924,7 +939,7 @@ def main():
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         "fwd_bwd_split": ("autograd step" if impl == "reference" else
                           "autograd fused step (losses.voxelize_gaussians_l1)"),
-        "autograd": autograd, "dropin": dropin,
+        "autograd": autograd, "dropin": dropin, "dropin_per_voxel": per_voxel,
         "e2e": {"value": evals_per_step / (e2e_ms / 1e3), "unit": UNIT,
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": st.step_in_bytes if st.fstep is not None else st.in_bytes,

@@ -57,7 +57,7 @@ UNIT = "evals/s"
 SMS = 148
 MUFU_PER_CLK = 16          # MUFU.EX2 throughput per SM per clock
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
-EXCHANGE = "nccl"  # halo exchange at N > 1 (--exchange)
+EXCHANGE = "p2p"  # halo exchange at N > 1 (--exchange)
 
 
 # ----------------------------------------------------------------- helpers
@@ -774,7 +774,7 @@ def main():
                          "(autograd, fused L1), dropin (voxelize_gaussians + torch "
                          "L1), voxel (dropin with the per-voxel backward), ssim "
                          "(dropin with 1 - fused_ssim3d)")
-    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="halo exchange at N > 1: direct writes into the peers' "
                          "symmetric receive buffers + device barriers (p2p), or "
                          "two NCCL all-to-alls per step")

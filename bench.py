@@ -774,6 +774,9 @@ def main():
                          "(autograd, fused L1), dropin (voxelize_gaussians + torch "
                          "L1), voxel (dropin with the per-voxel backward), ssim "
                          "(dropin with 1 - fused_ssim3d)")
+    ap.add_argument("--tc-backward", action="store_true",
+                    help="one-channel fused-L1 backward on the tensor-core engine "
+                         "(gsv_set_tensor_core_backward; off by default, slower)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="halo exchange at N > 1: direct writes into the peers' "
                          "symmetric receive buffers + device barriers (p2p), or "
@@ -782,6 +785,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     global EXCHANGE
     EXCHANGE = args.exchange
+    if args.tc_backward:
+        from gs_voxelizer_b200._lib import lib as _gl
+        _gl.gsv_set_tensor_core_backward(1)
 
     world, rank, local = setup_dist(args.gpus)
     impl = args.impl

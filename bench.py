@@ -9,8 +9,11 @@ N = 1 is BASELINE configuration 2: 256^3 volume, 100k Gaussians,
 sharded with per-GPU work fixed (weak scaling): a (256N, 256, 256) volume
 with N x 100k Gaussians, one 256^3 slab per rank; each rank owns the
 Gaussians whose centre lies in its slab and exchanges the boundary
-Gaussians (halo) with its peers, two NCCL all-to-alls per step
-(gs_voxelizer_b200.halo).
+Gaussians (halo) with its peers twice per step (gs_voxelizer_b200.halo):
+by direct writes into the peers' symmetric receive buffers and a device
+barrier, the whole step one CUDA graph (--exchange p2p, the default; NCCL
+all-to-alls if that cannot be set up), or by two NCCL all-to-alls
+(--exchange nccl).
 
 Metric: Gaussian-voxel evaluations per second over the whole step, counting
 each (Gaussian, voxel) pair once in the forward and once in the backward
@@ -205,6 +208,27 @@ def barrier(world):
 
 # ------------------------------------------------------------- step builders
 
+EXCHANGE_USED = None  # the halo exchange the N > 1 steps actually use
+
+
+def make_halo_step(cls, params, cfg, target, **kw):
+    """The owner-sharded step with the requested exchange; if setting up the
+    direct-write (p2p) exchange fails on this box (symmetric memory), the
+    NCCL all-to-all exchange instead, recorded in EXCHANGE_USED."""
+    global EXCHANGE_USED
+    if EXCHANGE == "p2p":
+        try:
+            step = cls(*params, cfg.vol, cfg.world, cfg.center, target,
+                       exchange="p2p", **kw)
+            EXCHANGE_USED = "p2p"
+            return step
+        except Exception as exc:  # reported in the JSON line
+            log(f"p2p exchange unavailable ({exc}); using NCCL all-to-alls")
+    EXCHANGE_USED = "nccl"
+    return cls(*params, cfg.vol, cfg.world, cfg.center, target,
+               exchange="nccl", **kw)
+
+
 class Step:
     """Holds device-resident leaves, target and the API used per step."""
 
@@ -257,10 +281,8 @@ class Step:
                 self.step_in_bytes = sum(h.numel() * h.element_size()
                                          for h in self.step_host)
                 self.params = [h.to(dev) for h in self.step_host]
-                self.fstep = HaloL1Step(*self.params, cfg.vol, cfg.world,
-                                        cfg.center, self.target,
-                                        denom=self.nvox_global,
-                                        exchange=EXCHANGE)
+                self.fstep = make_halo_step(HaloL1Step, self.params, cfg,
+                                            self.target, denom=self.nvox_global)
             else:
                 from gs_voxelizer_b200.step import FusedL1Step
                 self.params = [h.to(dev) for h in self.host]
@@ -659,8 +681,9 @@ def strong2048(world, rank, steps):
     class _Solo:
         rank, world = 0, 1
 
-    step = HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
-                      comm=None if world > 1 else _Solo(), exchange=EXCHANGE)
+    step = (make_halo_step(HaloL1Step, params, cfg, target) if world > 1 else
+            HaloL1Step(*params, cfg.vol, cfg.world, cfg.center, target,
+                       comm=_Solo()))
     for _ in range(2):
         step.run()
     E = evaluations(step.bins, cfg.vol, (tz0, tz1))
@@ -922,7 +945,7 @@ def main():
         "higher_is_better": True,
         "scaling": "strong" if strong else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded Gaussians + ellipsoid phantom)",
-        "config": {"workload": cfg.name, "vol_zyx": list(cfg.vol),
+        "config": {"workload": cfg.name, "exchange": EXCHANGE_USED, "vol_zyx": list(cfg.vol),
                    "gaussians": cfg.n, "channels": cfg.channels,
                    "intersections_per_gpu": n_isect,
                    "evals_per_step": evals_per_step,
@@ -935,11 +958,12 @@ def main():
                                  "kernels"),
                    "step": ("reference API through autograd" if impl == "reference"
                             else "gs_voxelizer_b200.halo.HaloL1Step: sync-free, "
-                                 "3 CUDA graphs around 2 exchanges ("
-                                 + ("direct writes into the peers' symmetric "
-                                    "receive buffers + device barriers"
-                                    if EXCHANGE == "p2p" else "NCCL all-to-alls")
-                                 + ")" if world > 1
+                                 + ("one CUDA graph per step, the 2 halo "
+                                    "exchanges as direct writes into the peers' "
+                                    "symmetric receive buffers + this library's "
+                                    "peer barrier" if EXCHANGE_USED == "p2p" else
+                                    "3 CUDA graphs around 2 NCCL all-to-alls")
+                                 if world > 1
                             else "gs_voxelizer_b200.step.FusedL1Step: sync-free, "
                                  "replayed as a CUDA graph")},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,

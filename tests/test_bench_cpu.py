@@ -52,3 +52,29 @@ def test_hbm_roofline_uses_measured_peak(tmp_path):
     assert r["peak_source"] == "measured hbm_gbs"
     r = b.hbm_roofline("forward", 0.18, 100, None, str(tmp_path / "missing.json"))
     assert r["peak"] == b.FALLBACK_HBM_GBS and r["peak_source"] == "fallback hbm_gbs"
+
+
+def test_halo_step_falls_back_to_nccl(monkeypatch):
+    """bench.make_halo_step: the p2p exchange when it can be set up, else the
+    NCCL exchange, and EXCHANGE_USED says which (no GPU: a stand-in class)."""
+    import bench
+
+    class Step:
+        def __init__(self, *args, exchange, **kw):
+            if exchange == "p2p" and Step.fail:
+                raise RuntimeError("no symmetric memory")
+            self.exchange, self.kw = exchange, kw
+
+    class Cfg:
+        vol, world, center = (8, 8, 8), (1.0, 1.0, 1.0), (0.5, 0.5, 0.5)
+
+    monkeypatch.setattr(bench, "EXCHANGE", "p2p")
+    Step.fail = False
+    s = bench.make_halo_step(Step, [1, 2, 3, 4], Cfg, "t", denom=3.0)
+    assert s.exchange == "p2p" and bench.EXCHANGE_USED == "p2p" and s.kw == {"denom": 3.0}
+    Step.fail = True
+    s = bench.make_halo_step(Step, [1, 2, 3, 4], Cfg, "t")
+    assert s.exchange == "nccl" and bench.EXCHANGE_USED == "nccl"
+    monkeypatch.setattr(bench, "EXCHANGE", "nccl")
+    Step.fail = False
+    assert bench.make_halo_step(Step, [1, 2, 3, 4], Cfg, "t").exchange == "nccl"
